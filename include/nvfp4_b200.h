@@ -1,0 +1,98 @@
+/* C ABI of libnvfp4_b200.so — B200 (sm_100a) NVFP4 block-scaled GEMV, GEMM and
+ * dual GEMM with a fused SiLU gate.
+ *
+ * These entry points replace the device work behind the reference's plugin
+ * boundary `custom_kernel(data) -> output` of the three problems under
+ * problems/nvidia/ (SwayamInSync/reference-kernels):
+ *
+ *   nvfp4_gemv       <- problems/nvidia/nvfp4_gemv/submission.py:28-54
+ *                       (torch._scaled_mm per batch, column 0 kept) and
+ *                       problems/nvidia/nvfp4_gemv/template_cute.py:199-247
+ *   nvfp4_gemm       <- problems/nvidia/nvfp4_gemm/submission.py:708-761
+ *                       (CuTe-DSL tcgen05 kernel launch)
+ *   nvfp4_dual_gemm  <- problems/nvidia/nvfp4_dual_gemm/submission.py:894-957
+ *
+ * Data layouts are the reference's input_t tensors (task.py of each problem),
+ * passed as raw device pointers: every operand is a stack of L contiguous
+ * batch slices, slice l starting at base + l * <x>_lstride.
+ *   packed e2m1 A/B : rows x K/2 bytes, two codes per byte, even K index in
+ *                     the low nibble (torch.float4_e2m1fn_x2)
+ *   plain scales    : rows x K/16 e4m3fn bytes, row-major (tuple slots 2-3)
+ *   blocked scales  : the 128x4-blocked order of to_blocked
+ *                     (nvfp4_gemm/reference.py:12-24), i.e. the memory order of
+ *                     the "permuted" tuple slots: byte (i, j) at
+ *                     (i/128)*(K/64)*512 + (j/4)*512 + (i%32)*16 + ((i%128)/32)*4 + j%4
+ *   C               : fp16, row m of slice l at c + l*c_lstride + m*ldc
+ *
+ * All calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ * default stream) and allocate nothing.  Every entry point returns 0 on
+ * success or one of the NVFP4_ERR_* codes; nvfp4_last_error() then returns a
+ * message (thread-local).  Nothing runs on the CPU: there is no fallback.
+ */
+#ifndef NVFP4_B200_H
+#define NVFP4_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  NVFP4_OK = 0,
+  NVFP4_ERR_SHAPE = 1,  /* unsupported size (see each function) */
+  NVFP4_ERR_ALIGN = 2,  /* pointer or stride alignment */
+  NVFP4_ERR_NULL = 3,   /* null pointer */
+  NVFP4_ERR_CUDA = 4,   /* launch / driver error (message has the CUDA string) */
+  NVFP4_ERR_DEVICE = 5, /* no current CUDA device */
+};
+
+/* Message for the last non-zero return on this thread. */
+const char* nvfp4_last_error(void);
+
+/* ABI revision of this header (1). */
+int nvfp4_abi_version(void);
+
+/* Reads (and optionally clears) the current device's status word, which the
+ * GEMM kernels set when a bounded pipeline wait runs out (1..4; 0 = ok).
+ * Synchronous.  Returns -1 on a CUDA error. */
+int nvfp4_device_status(int clear);
+
+/* Batched GEMV: c[m, l] = fp16( sum_k a[m,k,l]*sfa[m,k/16,l] * b[0,k,l]*sfb[0,k/16,l] ).
+ * Replaces the reference GEMV custom_kernel (nvfp4_gemv/submission.py:28-54).
+ *   a   : packed [L][M][K/2]            a_lstride   (bytes, multiple of 16)
+ *   b   : packed [L][rows>=1][K/2]      b_lstride   (bytes; the reference pads b to 128 rows)
+ *   sfa : plain  [L][M][K/16]           sfa_lstride (bytes)
+ *   sfb : plain  [L][rows>=1][K/16]     sfb_lstride (bytes)
+ *   c   : fp16   [L][M]                 c_lstride   (elements)
+ * Requires M % 4 == 0, K % 64 == 0 (the reference requires M % 128, K % 64). */
+int nvfp4_gemv(const void* a, const void* b, const void* sfa, const void* sfb, void* c, int M, int K, int L,
+               int64_t a_lstride, int64_t b_lstride, int64_t sfa_lstride, int64_t sfb_lstride, int64_t c_lstride,
+               void* stream);
+
+/* Batched block-scaled GEMM: C = (A*sfA) (B*sfB)^T, fp32 accumulation, fp16 out.
+ * Replaces nvfp4_gemm/submission.py:708-761.
+ *   a       : packed [L][M][K/2]    a_lstride   (bytes)
+ *   b       : packed [L][N][K/2]    b_lstride   (bytes)
+ *   sfa_blk : blocked scales of A   sfa_lstride (bytes, = M*K/16 for the reference tensors)
+ *   sfb_blk : blocked scales of B   sfb_lstride (bytes)
+ *   c       : fp16 [L][M][ldc]      ldc, c_lstride (elements)
+ * Requires M % 128 == 0, N % 128 == 0, K % 256 == 0 (task.yml of the problem),
+ * 16-byte aligned bases and batch strides.  An N-shard of a larger problem is
+ * passed as b + n0*K/2, sfb_blk + (n0/128)*K*8, c + n0 with ldc = full N. */
+int nvfp4_gemm(const void* a, const void* b, const void* sfa_blk, const void* sfb_blk, void* c, int M, int N, int K,
+               int L, int64_t a_lstride, int64_t b_lstride, int64_t sfa_lstride, int64_t sfb_lstride, int64_t ldc,
+               int64_t c_lstride, void* stream);
+
+/* Dual GEMM with fused gate: C = fp16( silu(A.B1^T) * (A.B2^T) ), both products
+ * in fp32.  Replaces nvfp4_dual_gemm/submission.py:894-957.  Same layouts and
+ * requirements as nvfp4_gemm; B1 and B2 share b_lstride / sfb_lstride. */
+int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* sfa_blk, const void* sfb1_blk,
+                    const void* sfb2_blk, void* c, int M, int N, int K, int L, int64_t a_lstride, int64_t b_lstride,
+                    int64_t sfa_lstride, int64_t sfb_lstride, int64_t ldc, int64_t c_lstride, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVFP4_B200_H */

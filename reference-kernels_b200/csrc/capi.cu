@@ -1,0 +1,197 @@
+// C ABI of libnvfp4_b200.so: plain pointers, sizes and strides; no torch types.
+// Declarations and the reference interface each entry point replaces are in
+// include/nvfp4_b200.h.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "../../include/nvfp4_b200.h"
+
+using namespace nvfp4;
+
+
+static thread_local char g_err[512] = "";
+
+static int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+// One device-resident status word per device; kernels record bounded-wait
+// timeouts here (0 = ok).
+static __device__ int g_status_word;
+
+static int* status_ptr(int dev) {
+  static int* ptrs[64] = {nullptr};
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+static int num_sms_of(int dev) {
+  static int cache[64] = {0};
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+#define NVFP4_API extern "C" __attribute__((visibility("default")))
+
+NVFP4_API const char* nvfp4_last_error(void) { return g_err; }
+
+NVFP4_API int nvfp4_abi_version(void) { return 1; }
+
+NVFP4_API int nvfp4_device_status(int clear) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_status_word, sizeof(int)) != cudaSuccess) return -1;
+  if (clear) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_status_word, &zero, sizeof(int));
+  }
+  return v;
+}
+
+NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa, const void* sfb, void* c, int M, int K, int L,
+               int64_t a_lstride, int64_t b_lstride, int64_t sfa_lstride, int64_t sfb_lstride, int64_t c_lstride,
+               void* stream) {
+  if (!a || !b || !sfa || !sfb || !c) return fail(NVFP4_ERR_NULL, "nvfp4_gemv: null pointer");
+  if (M <= 0 || K <= 0 || L <= 0) return fail(NVFP4_ERR_SHAPE, "nvfp4_gemv: M, K, L must be positive");
+  if (M % 4 != 0) return fail(NVFP4_ERR_SHAPE, "nvfp4_gemv: M=%d must be a multiple of 4", M);
+  if (K % 64 != 0) return fail(NVFP4_ERR_SHAPE, "nvfp4_gemv: K=%d must be a multiple of 64", K);
+  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sfa, 2) || !aligned(sfb, 2) || !aligned(c, 2) ||
+      (a_lstride % 16) || (b_lstride % 16) || (sfa_lstride % 2) || (sfb_lstride % 2))
+    return fail(NVFP4_ERR_ALIGN, "nvfp4_gemv: a/b need 16-byte, scales 2-byte alignment (bases and batch strides)");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4_ERR_DEVICE, "nvfp4_gemv: no CUDA device");
+  GemvParams p;
+  p.a = static_cast<const uint8_t*>(a);
+  p.b = static_cast<const uint8_t*>(b);
+  p.sfa = static_cast<const uint8_t*>(sfa);
+  p.sfb = static_cast<const uint8_t*>(sfb);
+  p.c = static_cast<__half*>(c);
+  p.M = M;
+  p.K = K;
+  p.L = L;
+  p.a_lstride = a_lstride;
+  p.b_lstride = b_lstride;
+  p.sfa_lstride = sfa_lstride;
+  p.sfb_lstride = sfb_lstride;
+  p.c_lstride = c_lstride;
+  p.ctas_per_l = 1;
+  cudaError_t e = launch_gemv(p, num_sms_of(dev), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: launch failed: %s", cudaGetErrorString(e));
+  return NVFP4_OK;
+}
+
+static int check_gemm_common(const char* name, const void* a, const void* b, const void* sfa, const void* sfb,
+                             const void* c, int M, int N, int K, int L, int64_t a_lstride, int64_t b_lstride,
+                             int64_t sfa_lstride, int64_t sfb_lstride, int64_t ldc, int64_t c_lstride) {
+  if (!a || !b || !sfa || !sfb || !c) return fail(NVFP4_ERR_NULL, "%s: null pointer", name);
+  if (M <= 0 || N <= 0 || K <= 0 || L <= 0) return fail(NVFP4_ERR_SHAPE, "%s: sizes must be positive", name);
+  if (M % 128 || N % 128)
+    return fail(NVFP4_ERR_SHAPE, "%s: M=%d and N=%d must be multiples of 128", name, M, N);
+  if (K % 256) return fail(NVFP4_ERR_SHAPE, "%s: K=%d must be a multiple of 256", name, K);
+  if (ldc < N) return fail(NVFP4_ERR_SHAPE, "%s: ldc=%lld < N=%d", name, (long long)ldc, N);
+  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sfa, 16) || !aligned(sfb, 16) || !aligned(c, 16) ||
+      (a_lstride % 16) || (b_lstride % 16) || (sfa_lstride % 16) || (sfb_lstride % 16) || (ldc % 8) ||
+      (c_lstride % 8))
+    return fail(NVFP4_ERR_ALIGN,
+                "%s: operands and scales need 16-byte aligned bases and batch strides; ldc and the C batch "
+                "stride must be multiples of 8",
+                name);
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_gemm(const void* a, const void* b, const void* sfa_blk, const void* sfb_blk, void* c, int M, int N, int K,
+               int L, int64_t a_lstride, int64_t b_lstride, int64_t sfa_lstride, int64_t sfb_lstride, int64_t ldc,
+               int64_t c_lstride, void* stream) {
+  int rc = check_gemm_common("nvfp4_gemm", a, b, sfa_blk, sfb_blk, c, M, N, K, L, a_lstride, b_lstride, sfa_lstride,
+                             sfb_lstride, ldc, c_lstride);
+  if (rc) return rc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4_ERR_DEVICE, "nvfp4_gemm: no CUDA device");
+  GemmArgs g{};
+  g.a = a;
+  g.b = b;
+  g.b2 = b;
+  g.sfa = sfa_blk;
+  g.sfb = sfb_blk;
+  g.sfb2 = sfb_blk;
+  g.c = c;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.L = L;
+  g.a_lstride = a_lstride;
+  g.b_lstride = b_lstride;
+  g.b2_lstride = b_lstride;
+  g.sfa_lstride = sfa_lstride;
+  g.sfb_lstride = sfb_lstride;
+  g.sfb2_lstride = sfb_lstride;
+  g.ldc = ldc;
+  g.c_lstride = c_lstride;
+  g.status = status_ptr(dev);
+  const char* why = nullptr;
+  cudaError_t e = launch_gemm(g, num_sms_of(dev), static_cast<cudaStream_t>(stream), &why);
+  if (e != cudaSuccess)
+    return fail(NVFP4_ERR_CUDA, "nvfp4_gemm: %s", why ? why : cudaGetErrorString(e));
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* sfa_blk, const void* sfb1_blk,
+                    const void* sfb2_blk, void* c, int M, int N, int K, int L, int64_t a_lstride, int64_t b_lstride,
+                    int64_t sfa_lstride, int64_t sfb_lstride, int64_t ldc, int64_t c_lstride, void* stream) {
+  int rc = check_gemm_common("nvfp4_dual_gemm", a, b1, sfa_blk, sfb1_blk, c, M, N, K, L, a_lstride, b_lstride,
+                             sfa_lstride, sfb_lstride, ldc, c_lstride);
+  if (rc) return rc;
+  if (!b2 || !sfb2_blk) return fail(NVFP4_ERR_NULL, "nvfp4_dual_gemm: null pointer");
+  if (!aligned(b2, 16) || !aligned(sfb2_blk, 16))
+    return fail(NVFP4_ERR_ALIGN, "nvfp4_dual_gemm: b2 and its scales need 16-byte alignment");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4_ERR_DEVICE, "nvfp4_dual_gemm: no CUDA device");
+  GemmArgs g{};
+  g.a = a;
+  g.b = b1;
+  g.b2 = b2;
+  g.sfa = sfa_blk;
+  g.sfb = sfb1_blk;
+  g.sfb2 = sfb2_blk;
+  g.c = c;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.L = L;
+  g.a_lstride = a_lstride;
+  g.b_lstride = b_lstride;
+  g.b2_lstride = b_lstride;
+  g.sfa_lstride = sfa_lstride;
+  g.sfb_lstride = sfb_lstride;
+  g.sfb2_lstride = sfb_lstride;
+  g.ldc = ldc;
+  g.c_lstride = c_lstride;
+  g.status = status_ptr(dev);
+  const char* why = nullptr;
+  cudaError_t e = launch_dual_gemm(g, num_sms_of(dev), static_cast<cudaStream_t>(stream), &why);
+  if (e != cudaSuccess)
+    return fail(NVFP4_ERR_CUDA, "nvfp4_dual_gemm: %s", why ? why : cudaGetErrorString(e));
+  return NVFP4_OK;
+}
+

@@ -1,0 +1,191 @@
+// NVFP4 block-scaled GEMV for sm_100a:  c[m, l] = sum_k (a[m,k,l] sfa[m,k/16,l]) (b[k,l] sfb[k/16,l])
+//
+// Semantics follow ref_kernel of problems/nvidia/nvfp4_gemv/reference.py:28-54
+// (column 0 of a block-scaled GEMM with fp32 accumulation, fp16 output).
+//
+// The kernel is HBM-bound on the packed A stream (K/2 bytes per row plus K/16
+// scale bytes), so it is written as a streaming kernel, not a tensor-core one:
+//   * one persistent CTA range of rows per (CTA, l); ranges differ by at most
+//     one quad of rows, so every SM streams the same number of bytes;
+//   * within a CTA the warps split K into 512-byte segments (one 16-byte
+//     ld.global.nc per lane per row) and every warp streams up to 8 rows at
+//     once, so each lane keeps eight 128-bit loads in flight;
+//   * e2m1 pairs are widened with cvt.rn.f16x2.e2m1x2 and multiplied against
+//     the (unscaled) e2m1 values of b with HFMA2: the products of two e2m1
+//     values are multiples of 1/4 below 36, so the 8-term sums per f16 half
+//     are exact; the group sum is then scaled in fp32 by sfa*sfb (an exact
+//     product of two e4m3 values) and accumulated in fp32;
+//   * per-warp partial sums are folded across lanes with a 9-shuffle
+//     halving butterfly and across warps through shared memory.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace nvfp4 {
+
+
+
+constexpr int kGemvRowsPerBatch = 8;
+constexpr int kGemvMaxWarps = 16;
+
+__device__ __forceinline__ uint4 ld_stream_16(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Dot product of 32 e2m1 values (16 bytes) with 32 f16 values of b for two
+// 16-element groups; returns group sums g0, g1 (exact, in fp32).
+__device__ __forceinline__ float2 group_sums(const uint4 av, const uint32_t (&bh)[16]) {
+  const uint32_t w[4] = {av.x, av.y, av.z, av.w};
+  __half2 acc0 = __float2half2_rn(0.f), acc1 = __float2half2_rn(0.f);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    uint32_t h[4];
+    e2m1x8_to_f16x2x4(w[i], h);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      acc0 = __hfma2(*reinterpret_cast<__half2*>(&h[j]), *reinterpret_cast<const __half2*>(&bh[i * 4 + j]), acc0);
+  }
+#pragma unroll
+  for (int i = 2; i < 4; ++i) {
+    uint32_t h[4];
+    e2m1x8_to_f16x2x4(w[i], h);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      acc1 = __hfma2(*reinterpret_cast<__half2*>(&h[j]), *reinterpret_cast<const __half2*>(&bh[i * 4 + j]), acc1);
+  }
+  const float2 f0 = __half22float2(acc0), f1 = __half22float2(acc1);
+  return make_float2(f0.x + f0.y, f1.x + f1.y);
+}
+
+__device__ __forceinline__ float2 e4m3_pair(uint16_t codes) {
+  uint32_t h = e4m3x2_to_f16x2(codes);
+  return __half22float2(*reinterpret_cast<__half2*>(&h));
+}
+
+__global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvParams p) {
+  __shared__ float red[2][kGemvMaxWarps][kGemvRowsPerBatch];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int l = blockIdx.y;
+  const int K2 = p.K >> 1, SK = p.K >> 4;
+  const int nseg = (K2 + 511) >> 9;
+
+  // Row range of this CTA, in quads of rows.
+  const int quads = p.M >> 2;
+  const int q0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * quads) / p.ctas_per_l);
+  const int q1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * quads) / p.ctas_per_l);
+
+  const uint8_t* a_l = p.a + l * p.a_lstride;
+  const uint8_t* sfa_l = p.sfa + l * p.sfa_lstride;
+  const uint8_t* b_l = p.b + l * p.b_lstride;
+  const uint8_t* sfb_l = p.sfb + l * p.sfb_lstride;
+
+  // b of the first segment of this warp stays in registers while the warp
+  // owns exactly one segment (K <= 16 * 1024 with 16 warps).
+  uint32_t bh[16];
+  float sb0 = 0.f, sb1 = 0.f;
+  int cached_seg = -1;
+
+  int buf = 0;
+  for (int qb = q0; qb < q1; qb += 2, buf ^= 1) {
+    const int row0 = qb * 4;
+    const int nrows = (q1 - qb >= 2) ? 8 : 4;
+    float part[kGemvRowsPerBatch];
+#pragma unroll
+    for (int r = 0; r < kGemvRowsPerBatch; ++r) part[r] = 0.f;
+
+    for (int seg = warp; seg < nseg; seg += nwarps) {
+      const int kb = seg * 512 + lane * 16;  // byte offset in the row
+      if (kb >= K2) continue;
+      if (seg != cached_seg) {
+        const uint4 bv = *reinterpret_cast<const uint4*>(b_l + kb);
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint32_t h[4];
+          e2m1x8_to_f16x2x4(bw[i], h);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) bh[i * 4 + j] = h[j];
+        }
+        const float2 sb = e4m3_pair(*reinterpret_cast<const uint16_t*>(sfb_l + (kb >> 3)));
+        sb0 = sb.x;
+        sb1 = sb.y;
+        cached_seg = seg;
+      }
+      uint4 av[kGemvRowsPerBatch];
+      uint16_t sa[kGemvRowsPerBatch];
+#pragma unroll
+      for (int r = 0; r < kGemvRowsPerBatch; ++r) {
+        if (r < nrows) {
+          av[r] = ld_stream_16(a_l + static_cast<int64_t>(row0 + r) * K2 + kb);
+          sa[r] = __ldg(reinterpret_cast<const uint16_t*>(sfa_l + static_cast<int64_t>(row0 + r) * SK + (kb >> 3)));
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kGemvRowsPerBatch; ++r) {
+        if (r < nrows) {
+          const float2 g = group_sums(av[r], bh);
+          const float2 s = e4m3_pair(sa[r]);
+          part[r] = fmaf(g.x, s.x * sb0, part[r]);
+          part[r] = fmaf(g.y, s.y * sb1, part[r]);
+        }
+      }
+    }
+
+    // Halving butterfly: after it, lane j holds the warp total of row
+    // 4*bit4(j) + 2*bit3(j) + bit2(j).
+    const bool up16 = lane & 16, up8 = lane & 8, up4 = lane & 4;
+    float v4[4], v2[2], v1;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = up16 ? part[i] : part[4 + i];
+      const float keep = up16 ? part[4 + i] : part[i];
+      v4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = up8 ? v4[i] : v4[2 + i];
+      const float keep = up8 ? v4[2 + i] : v4[i];
+      v2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    {
+      const float send = up4 ? v2[0] : v2[1];
+      const float keep = up4 ? v2[1] : v2[0];
+      v1 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
+    v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+    if ((lane & 3) == 0) red[buf][warp][(up16 ? 4 : 0) + (up8 ? 2 : 0) + (up4 ? 1 : 0)] = v1;
+    __syncthreads();
+    if (threadIdx.x < nrows) {
+      float s = 0.f;
+      for (int w = 0; w < nwarps; ++w) s += red[buf][w][threadIdx.x];
+      p.c[l * p.c_lstride + row0 + threadIdx.x] = __float2half_rn(s);
+    }
+  }
+}
+
+// Host launcher (called from the C ABI in capi.cu).
+cudaError_t launch_gemv(const GemvParams& in, int num_sms, cudaStream_t stream) {
+  GemvParams p = in;
+  const int K2 = p.K / 2;
+  const int nseg = (K2 + 511) / 512;
+  const int nwarps = nseg < kGemvMaxWarps ? nseg : kGemvMaxWarps;
+  // Aim for ~32 resident warps per SM over the whole grid, one CTA range per (x, l).
+  int ctas_per_sm = 32 / nwarps;
+  if (ctas_per_sm < 1) ctas_per_sm = 1;
+  int total = num_sms * ctas_per_sm;
+  int per_l = total / p.L;
+  if (per_l < 1) per_l = 1;
+  const int quads = p.M / 4;
+  if (per_l > quads) per_l = quads;
+  p.ctas_per_l = per_l;
+  dim3 grid(per_l, p.L), block(nwarps * 32);
+  gemv_kernel<<<grid, block, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace nvfp4

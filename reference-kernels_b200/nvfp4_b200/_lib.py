@@ -1,0 +1,67 @@
+"""Loader for libnvfp4_b200.so (the C ABI declared in include/nvfp4_b200.h).
+
+The shared library is built in-tree by ``build.py`` / ``csrc/Makefile``.  There
+is no CPU fallback: if the library or a CUDA device is missing, every call
+raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libnvfp4_b200.so")
+
+EXPORTS = (
+    "nvfp4_last_error",
+    "nvfp4_abi_version",
+    "nvfp4_device_status",
+    "nvfp4_gemv",
+    "nvfp4_gemm",
+    "nvfp4_dual_gemm",
+)
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_L = ctypes.c_int64
+
+_lib = None
+
+
+class Nvfp4Error(RuntimeError):
+    """Raised when an entry point of libnvfp4_b200.so returns a non-zero code."""
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise Nvfp4Error(
+            f"{LIB_PATH} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'` "
+            "(nvcc, sm_100a); there is no CPU fallback")
+    lib = ctypes.CDLL(LIB_PATH)
+    lib.nvfp4_last_error.restype = ctypes.c_char_p
+    lib.nvfp4_last_error.argtypes = []
+    lib.nvfp4_abi_version.restype = _I
+    lib.nvfp4_device_status.restype = _I
+    lib.nvfp4_device_status.argtypes = [_I]
+    lib.nvfp4_gemv.restype = _I
+    lib.nvfp4_gemv.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _L, _P]
+    lib.nvfp4_gemm.restype = _I
+    lib.nvfp4_gemm.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _P]
+    lib.nvfp4_dual_gemm.restype = _I
+    lib.nvfp4_dual_gemm.argtypes = [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _P]
+    _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        msg = load().nvfp4_last_error().decode(errors="replace")
+        raise Nvfp4Error(f"libnvfp4_b200 error {rc}: {msg}")
+
+
+def device_status(clear: bool = True) -> int:
+    """Device status word (bounded-wait timeouts in the GEMM kernels); 0 = ok."""
+    return load().nvfp4_device_status(1 if clear else 0)

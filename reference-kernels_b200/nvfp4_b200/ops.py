@@ -1,0 +1,130 @@
+"""``custom_kernel`` drop-ins for the three NVFP4 problems.
+
+Each function keeps the reference's plugin contract ``custom_kernel(data:
+input_t) -> output_t`` (``problems/nvidia/<problem>/task.py``): it takes the
+tuple produced by ``generate_input``, launches the sm_100a kernel on the
+current CUDA stream, writes into the preallocated output ``c`` and returns it.
+Tensors are read through their data pointers and strides; nothing is copied,
+allocated or synchronised on the call path.
+
+Reference entry points replaced:
+  gemv       problems/nvidia/nvfp4_gemv/submission.py:28-54 (and template_cute.py:199-247)
+  gemm       problems/nvidia/nvfp4_gemm/submission.py:708-761
+  dual_gemm  problems/nvidia/nvfp4_dual_gemm/submission.py:894-957
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _lib
+
+_CHECK_STATUS = os.environ.get("NVFP4_CHECK_STATUS", "0") == "1"
+
+
+def _stream_ptr(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise _lib.Nvfp4Error(msg)
+
+
+def _check_operand(t: torch.Tensor, name: str) -> None:
+    # [rows, K/2, L] view of contiguous (L, rows, K/2) storage (task.py input_t)
+    _require(t.is_cuda, f"{name} must be a CUDA tensor (no CPU fallback)")
+    _require(t.element_size() == 1, f"{name} must be packed fp4x2 / uint8")
+    _require(t.stride(1) == 1 and t.stride(0) == t.shape[1],
+             f"{name} must have K-major rows (strides {t.stride()})")
+
+
+def _blocked_lstride(t: torch.Tensor, rows: int, sk: int, name: str) -> int:
+    """Batch stride (bytes) of a permuted / blocked scale view; validates its strides."""
+    _require(t.is_cuda and t.element_size() == 1, f"{name} must be fp8-e4m3 / uint8 on CUDA")
+    kk = sk // 4
+    if t.dim() == 6:
+        # (32, 4, rows/128, 4, SK/4, L) view of (L, rows/128, SK/4, 32, 4, 4) storage
+        _require(tuple(t.shape[:5]) == (32, 4, rows // 128, 4, kk),
+                 f"{name}: blocked scale shape {tuple(t.shape)} does not match rows={rows}, K/16={sk}")
+        _require(t.stride()[:5] == (16, 4, kk * 512, 1, 512),
+                 f"{name}: blocked scales must be the reference's permuted view (strides {t.stride()})")
+        return t.stride(5)
+    # flat blocked vector (to_blocked output) for L == 1
+    _require(t.dim() == 1 and t.numel() == rows * sk and t.stride(0) == 1,
+             f"{name}: expected a (32,4,*,4,*,L) permuted view or a flat to_blocked vector")
+    return rows * sk
+
+
+def _post():
+    if _CHECK_STATUS:
+        torch.cuda.synchronize()
+        st = _lib.device_status(True)
+        if st != 0:
+            raise _lib.Nvfp4Error(f"kernel pipeline wait timed out (device status {st})")
+
+
+def gemv(data):
+    """custom_kernel for nvfp4_gemv: reads a, b, sfa, sfb (plain scales) and writes c[:, 0, :]."""
+    a, b, sfa, sfb, _sfa_p, _sfb_p, c = data
+    m, k2, l = a.shape
+    k = 2 * k2
+    _check_operand(a, "a")
+    _require(b.is_cuda and b.stride(1) == 1 and b.shape[1] == k2 and b.shape[2] == l, "b must be [rows, K/2, L]")
+    _require(sfa.stride(1) == 1 and sfa.stride(0) == k // 16 and tuple(sfa.shape) == (m, k // 16, l),
+             f"sfa must be plain [M, K/16, L] with unit inner stride (strides {sfa.stride()})")
+    _require(sfb.stride(1) == 1 and sfb.shape[1] == k // 16, "sfb must be plain [rows, K/16, L]")
+    _require(c.dtype == torch.float16 and tuple(c.shape) == (m, 1, l), "c must be fp16 [M, 1, L]")
+    lib = _lib.load()
+    _lib.check(lib.nvfp4_gemv(
+        a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), c.data_ptr(),
+        m, k, l, a.stride(2), b.stride(2), sfa.stride(2), sfb.stride(2), c.stride(2),
+        _stream_ptr(a)))
+    _post()
+    return c
+
+
+def gemm(data):
+    """custom_kernel for nvfp4_gemm: reads a, b and the blocked (permuted) scales, writes c."""
+    a, b, _sfa, _sfb, sfa_p, sfb_p, c = data
+    m, k2, l = a.shape
+    n = b.shape[0]
+    k = 2 * k2
+    _check_operand(a, "a")
+    _check_operand(b, "b")
+    _require(c.dtype == torch.float16 and tuple(c.shape) == (m, n, l) and c.stride(1) == 1,
+             "c must be fp16 [M, N, L] with unit column stride")
+    sa = _blocked_lstride(sfa_p, m, k // 16, "sfa_permuted")
+    sb = _blocked_lstride(sfb_p, n, k // 16, "sfb_permuted")
+    lib = _lib.load()
+    _lib.check(lib.nvfp4_gemm(
+        a.data_ptr(), b.data_ptr(), sfa_p.data_ptr(), sfb_p.data_ptr(), c.data_ptr(),
+        m, n, k, l, a.stride(2), b.stride(2), sa, sb, c.stride(0), c.stride(2), _stream_ptr(a)))
+    _post()
+    return c
+
+
+def dual_gemm(data):
+    """custom_kernel for nvfp4_dual_gemm: c = fp16(silu(A.B1^T) * (A.B2^T))."""
+    a, b1, b2, _sfa, _sfb1, _sfb2, sfa_p, sfb1_p, sfb2_p, c = data
+    m, k2, l = a.shape
+    n = b1.shape[0]
+    k = 2 * k2
+    _check_operand(a, "a")
+    _check_operand(b1, "b1")
+    _check_operand(b2, "b2")
+    _require(b1.stride(2) == b2.stride(2), "b1 and b2 must share their batch stride")
+    _require(c.dtype == torch.float16 and tuple(c.shape) == (m, n, l) and c.stride(1) == 1,
+             "c must be fp16 [M, N, L] with unit column stride")
+    sa = _blocked_lstride(sfa_p, m, k // 16, "sfa_permuted")
+    sb1 = _blocked_lstride(sfb1_p, n, k // 16, "sfb1_permuted")
+    sb2 = _blocked_lstride(sfb2_p, n, k // 16, "sfb2_permuted")
+    _require(sb1 == sb2, "sfb1 and sfb2 must share their batch stride")
+    lib = _lib.load()
+    _lib.check(lib.nvfp4_dual_gemm(
+        a.data_ptr(), b1.data_ptr(), b2.data_ptr(), sfa_p.data_ptr(), sfb1_p.data_ptr(), sfb2_p.data_ptr(),
+        c.data_ptr(), m, n, k, l, a.stride(2), b1.stride(2), sa, sb1, c.stride(0), c.stride(2),
+        _stream_ptr(a)))
+    _post()
+    return c

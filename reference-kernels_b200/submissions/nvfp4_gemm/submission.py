@@ -1,0 +1,25 @@
+"""Drop-in ``submission.py`` for problems/nvidia/nvfp4_gemm.
+
+Copy (or symlink) this file as ``submission.py`` next to the problem's
+reference.py / task.py / utils.py / eval harness; it needs the directory
+``reference-kernels_b200`` importable, which is found relative to this file
+or through the NVFP4_B200_HOME environment variable.
+"""
+import os
+import sys
+
+_home = os.environ.get("NVFP4_B200_HOME",
+                       os.path.abspath(os.path.join(os.path.dirname(os.path.realpath(__file__)), "..", "..")))
+if _home not in sys.path:
+    sys.path.insert(0, _home)
+
+from nvfp4_b200.ops import gemm as _impl  # noqa: E402
+
+
+def compile_kernel():
+    """The kernels are compiled ahead of time (libnvfp4_b200.so); nothing to do."""
+    return None
+
+
+def custom_kernel(data):
+    return _impl(data)
