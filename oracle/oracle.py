@@ -195,12 +195,30 @@ def allclose_report(received, expected, rtol=1e-3, atol=1e-3, max_print=5) -> li
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the reference's dequantise-to-fp32 then fp32-matmul path,
-# multithreaded through torch's CPU BLAS.  Used by bench.py only.
+# CPU port of ref_kernel for timing (bench.py's cpu_baseline and reference
+# arm only): dequantise through the 256-entry byte -> (lo, hi) table and the
+# e4m3 table into fp32, then an fp32 matmul, multithreaded through torch's
+# CPU kernels -- the arithmetic of reference.py (dequantise to fp32, fp32
+# GEMM, fp16 cast), run on host cores.
 # ---------------------------------------------------------------------------
 
-def cpu_baseline_gemm_f32(a, b, sfa, sfb):
+def torch_dequant(packed, scales):
+    """packed [rows, K/2] uint8 tensor, scales [rows, K/16] uint8 codes -> fp32 [rows, K]."""
     import torch
-    da = torch.from_numpy(dequant(a, sfa))
-    db = torch.from_numpy(dequant(b, sfb))
-    return (da @ db.T).to(torch.float16)
+    rows, k2 = packed.shape
+    vals = torch.from_numpy(_PAIR_TABLE)[packed.long()].reshape(rows, 2 * k2)
+    sf = torch.from_numpy(E4M3FN_VALUES)[scales.long()]
+    return (vals.view(rows, -1, SF_VEC) * sf.unsqueeze(-1)).view(rows, 2 * k2)
+
+
+def cpu_port(problem: str, a, b, sfa, sfb, b2=None, sfb2=None):
+    """One batch index on the CPU: a/b/b2 packed uint8, sf* plain uint8 codes -> fp16."""
+    import torch
+    da = torch_dequant(a, sfa)
+    if problem == "gemv":
+        return (da @ torch_dequant(b[:1], sfb[:1])[0]).to(torch.float16)
+    r1 = da @ torch_dequant(b, sfb).T
+    if problem == "gemm":
+        return r1.to(torch.float16)
+    r2 = da @ torch_dequant(b2, sfb2).T
+    return (torch.nn.functional.silu(r1) * r2).to(torch.float16)
