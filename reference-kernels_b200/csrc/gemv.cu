@@ -65,6 +65,26 @@ __device__ __forceinline__ float2 e4m3_pair(uint16_t codes) {
   return __half22float2(*reinterpret_cast<__half2*>(&h));
 }
 
+// One work item = (batch of up to 8 rows, one 512-byte K segment of this warp).
+struct GemvItem {
+  uint4 av[kGemvRowsPerBatch];
+  uint16_t sa[kGemvRowsPerBatch];
+};
+
+__device__ __forceinline__ void load_item(GemvItem& it, const uint8_t* a_l, const uint8_t* sfa_l, int row0, int nrows,
+                                          int kb, int K2, int SK) {
+#pragma unroll
+  for (int r = 0; r < kGemvRowsPerBatch; ++r) {
+    if (r < nrows && kb < K2) {
+      it.av[r] = ld_stream_16(a_l + static_cast<int64_t>(row0 + r) * K2 + kb);
+      it.sa[r] = __ldg(reinterpret_cast<const uint16_t*>(sfa_l + static_cast<int64_t>(row0 + r) * SK + (kb >> 3)));
+    } else {
+      it.av[r] = make_uint4(0, 0, 0, 0);
+      it.sa[r] = 0;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvParams p) {
   __shared__ float red[2][kGemvMaxWarps][kGemvRowsPerBatch];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -72,67 +92,85 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvPara
   const int l = blockIdx.y;
   const int K2 = p.K >> 1, SK = p.K >> 4;
   const int nseg = (K2 + 511) >> 9;
+  const int my_segs = (nseg - warp + nwarps - 1) / nwarps;  // segments seg = warp + j*nwarps
 
   // Row range of this CTA, in quads of rows.
   const int quads = p.M >> 2;
   const int q0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * quads) / p.ctas_per_l);
   const int q1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * quads) / p.ctas_per_l);
+  const int nbatch = (q1 - q0 + 1) >> 1;
 
   const uint8_t* a_l = p.a + l * p.a_lstride;
   const uint8_t* sfa_l = p.sfa + l * p.sfa_lstride;
   const uint8_t* b_l = p.b + l * p.b_lstride;
   const uint8_t* sfb_l = p.sfb + l * p.sfb_lstride;
 
-  // b of the first segment of this warp stays in registers while the warp
-  // owns exactly one segment (K <= 16 * 1024 with 16 warps).
+  // b of the current segment (unscaled e2m1 as f16 pairs) and its two scales.
   uint32_t bh[16];
   float sb0 = 0.f, sb1 = 0.f;
   int cached_seg = -1;
 
+  // Items are visited batch-major, segment-minor; item i+1 is loaded while
+  // item i is being reduced, so every lane keeps 8 loads in flight across the
+  // per-batch barrier.
+  const int nitems = nbatch * my_segs;
+  GemvItem cur, nxt;
+  auto item_coords = [&](int i, int& row0, int& nrows, int& seg) {
+    const int bi = i / my_segs;
+    const int j = i - bi * my_segs;
+    const int qb = q0 + 2 * bi;
+    row0 = qb * 4;
+    nrows = (q1 - qb >= 2) ? 8 : 4;
+    seg = warp + j * nwarps;
+  };
+  if (nitems > 0) {
+    int row0, nrows, seg;
+    item_coords(0, row0, nrows, seg);
+    load_item(cur, a_l, sfa_l, row0, nrows, seg * 512 + lane * 16, K2, SK);
+  }
+  float part[kGemvRowsPerBatch];
+#pragma unroll
+  for (int r = 0; r < kGemvRowsPerBatch; ++r) part[r] = 0.f;
   int buf = 0;
-  for (int qb = q0; qb < q1; qb += 2, buf ^= 1) {
-    const int row0 = qb * 4;
-    const int nrows = (q1 - qb >= 2) ? 8 : 4;
-    float part[kGemvRowsPerBatch];
-#pragma unroll
-    for (int r = 0; r < kGemvRowsPerBatch; ++r) part[r] = 0.f;
-
-    for (int seg = warp; seg < nseg; seg += nwarps) {
-      const int kb = seg * 512 + lane * 16;  // byte offset in the row
-      if (kb >= K2) continue;
-      if (seg != cached_seg) {
-        const uint4 bv = *reinterpret_cast<const uint4*>(b_l + kb);
-        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint32_t h[4];
-          e2m1x8_to_f16x2x4(bw[i], h);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) bh[i * 4 + j] = h[j];
-        }
-        const float2 sb = e4m3_pair(*reinterpret_cast<const uint16_t*>(sfb_l + (kb >> 3)));
-        sb0 = sb.x;
-        sb1 = sb.y;
-        cached_seg = seg;
+  // Warps with no segment (nseg < nwarps never happens; guard anyway) still join the barriers.
+  const int total_batches = nbatch;
+  int item = 0;
+  for (int bi = 0; bi < total_batches; ++bi) {
+    int row0 = (q0 + 2 * bi) * 4;
+    const int nrows = (q1 - (q0 + 2 * bi) >= 2) ? 8 : 4;
+    for (int j = 0; j < my_segs; ++j, ++item) {
+      if (item + 1 < nitems) {
+        int r1, n1, s1;
+        item_coords(item + 1, r1, n1, s1);
+        load_item(nxt, a_l, sfa_l, r1, n1, s1 * 512 + lane * 16, K2, SK);
       }
-      uint4 av[kGemvRowsPerBatch];
-      uint16_t sa[kGemvRowsPerBatch];
+      const int seg = warp + j * nwarps;
+      const int kb = seg * 512 + lane * 16;
+      if (kb < K2) {
+        if (seg != cached_seg) {
+          const uint4 bv = *reinterpret_cast<const uint4*>(b_l + kb);
+          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-      for (int r = 0; r < kGemvRowsPerBatch; ++r) {
-        if (r < nrows) {
-          av[r] = ld_stream_16(a_l + static_cast<int64_t>(row0 + r) * K2 + kb);
-          sa[r] = __ldg(reinterpret_cast<const uint16_t*>(sfa_l + static_cast<int64_t>(row0 + r) * SK + (kb >> 3)));
+          for (int i = 0; i < 4; ++i) {
+            uint32_t h[4];
+            e2m1x8_to_f16x2x4(bw[i], h);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) bh[i * 4 + q] = h[q];
+          }
+          const float2 sb = e4m3_pair(*reinterpret_cast<const uint16_t*>(sfb_l + (kb >> 3)));
+          sb0 = sb.x;
+          sb1 = sb.y;
+          cached_seg = seg;
         }
-      }
 #pragma unroll
-      for (int r = 0; r < kGemvRowsPerBatch; ++r) {
-        if (r < nrows) {
-          const float2 g = group_sums(av[r], bh);
-          const float2 s = e4m3_pair(sa[r]);
+        for (int r = 0; r < kGemvRowsPerBatch; ++r) {
+          const float2 g = group_sums(cur.av[r], bh);
+          const float2 s = e4m3_pair(cur.sa[r]);
           part[r] = fmaf(g.x, s.x * sb0, part[r]);
           part[r] = fmaf(g.y, s.y * sb1, part[r]);
         }
       }
+      cur = nxt;
     }
 
     // Halving butterfly: after it, lane j holds the warp total of row
@@ -159,25 +197,37 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvPara
     v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
     v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
     if ((lane & 3) == 0) red[buf][warp][(up16 ? 4 : 0) + (up8 ? 2 : 0) + (up4 ? 1 : 0)] = v1;
+#pragma unroll
+    for (int r = 0; r < kGemvRowsPerBatch; ++r) part[r] = 0.f;
     __syncthreads();
     if (threadIdx.x < nrows) {
       float s = 0.f;
       for (int w = 0; w < nwarps; ++w) s += red[buf][w][threadIdx.x];
       p.c[l * p.c_lstride + row0 + threadIdx.x] = __float2half_rn(s);
     }
+    buf ^= 1;
   }
 }
 
-// Host launcher (called from the C ABI in capi.cu).
+// Host launcher (called from the C ABI in capi.cu).  The grid is exactly the
+// number of CTAs that can be resident at once, split evenly over the L batch
+// indices, so every CTA streams the same number of rows in a single wave.
 cudaError_t launch_gemv(const GemvParams& in, int num_sms, cudaStream_t stream) {
   GemvParams p = in;
   const int K2 = p.K / 2;
   const int nseg = (K2 + 511) / 512;
   const int nwarps = nseg < kGemvMaxWarps ? nseg : kGemvMaxWarps;
-  // Aim for ~32 resident warps per SM over the whole grid, one CTA range per (x, l).
-  int ctas_per_sm = 32 / nwarps;
-  if (ctas_per_sm < 1) ctas_per_sm = 1;
-  int total = num_sms * ctas_per_sm;
+  static int occ_cache[kGemvMaxWarps + 1] = {0};
+  if (!occ_cache[nwarps]) {
+    int occ = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_kernel, nwarps * 32, 0);
+    if (e != cudaSuccess) return e;
+    occ_cache[nwarps] = occ > 0 ? occ : 1;
+  }
+  int ctas_per_sm = occ_cache[nwarps];
+  // More than ~48 warps per SM only adds barrier traffic.
+  while (ctas_per_sm > 1 && ctas_per_sm * nwarps > 48) --ctas_per_sm;
+  const int total = num_sms * ctas_per_sm;
   int per_l = total / p.L;
   if (per_l < 1) per_l = 1;
   const int quads = p.M / 4;
