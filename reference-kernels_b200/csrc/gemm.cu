@@ -5,25 +5,32 @@
 //   Dual:  C[m,n,l] = fp16( silu(A.B1^T) * (A.B2^T) ), both products in fp32
 //          ref_kernel of problems/nvidia/nvfp4_dual_gemm/reference.py:27-77
 //
-// Structure (one CTA per SM, persistent, 6 warps):
+// Structure (one CTA per SM, persistent, 7 warps):
 //   warp 0      TMA producer: A/B tiles with 128-byte swizzle through
 //               cp.async.bulk.tensor, the 128x4-blocked scale factors through
 //               plain cp.async.bulk (each 128-row block of scales for a
 //               256-wide K tile is one contiguous 2 KB run), into a ring of
 //               kStages shared-memory stages guarded by full/empty mbarriers.
-//   warp 1      TMEM owner and MMA issuer: per K tile, tcgen05.cp moves the
-//               stage's scale blocks into TMEM (32x128b, replicated to the
-//               four lane quarters), then four tcgen05.mma kind::mxf4nvf4
-//               (M=128, N=kBN, K=64 each; two per step for the dual GEMM,
-//               sharing the A tile) accumulate in fp32 in TMEM;
+//   warp 6      scale copier: per K tile, tcgen05.cp moves the stage's scale
+//               blocks into TMEM (32x128b, replicated to the four lane
+//               quarters) and commits to sf_ready[stage].  Copies issued by
+//               the MMA thread itself would serialise with its MMAs in the
+//               tensor pipe (measured ~45 cycles per copy); from a second
+//               thread they overlap with the MMAs.
+//   warp 1      TMEM owner and MMA issuer: per K tile, four tcgen05.mma
+//               kind::mxf4nvf4 (M=128, N=BN, K=64 each; two per step for the
+//               dual GEMM, sharing the A tile) accumulate in fp32 in TMEM;
 //               tcgen05.commit releases the stage and, after the last K tile,
 //               hands the accumulator to the epilogue.
 //   warps 2..5  epilogue: tcgen05.ld rows of the accumulator(s), optional
 //               silu(x)*y in fp32, fp16 conversion, 16-byte global stores.
-// The GEMM double-buffers its accumulator in TMEM so the epilogue of tile i
-// overlaps the main loop of tile i+1.  No load uses cluster multicast.
+// With BN=128 the GEMM double-buffers its accumulator in TMEM so the epilogue
+// of tile i overlaps the main loop of tile i+1; BN=256 and the dual GEMM need
+// all accumulator columns for one tile.  No load uses cluster multicast.
 #include "common.cuh"
 #include "kernels.h"
+
+#include <cstdlib>
 
 namespace nvfp4 {
 
@@ -33,7 +40,7 @@ constexpr int kBKBytes = kBK / 2;
 constexpr int kMmaK = 64;         // K per tcgen05.mma for kind::mxf4nvf4
 constexpr int kSfBlockBytes = 512;  // one 128-row x 4-scale block
 constexpr int kSfStageBytes = kSfBlockBytes * (kBK / kMmaK);  // 2 KB per operand per stage
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;
 
 template <int BN, bool kDual>
 struct GemmConfig {
@@ -42,8 +49,8 @@ struct GemmConfig {
   static constexpr int kBBytes = BN * kBKBytes;
   static constexpr int kStageBytes = kABytes + kNB * kBBytes;
   static constexpr int kSfOps = 1 + kNB * (BN / 128);                // 2 KB scale runs per stage
-  static constexpr int kStages = kDual ? 4 : 5;
-  static constexpr int kAccBufs = kDual ? 1 : 2;
+  static constexpr int kStages = (kDual || BN == 256) ? 4 : 5;
+  static constexpr int kAccBufs = (kDual || BN == 256) ? 1 : 2;
   static constexpr int kAccCols = kNB * BN;                           // fp32 columns per accumulator buffer
   static constexpr int kSfCols = 16 * kSfOps;                         // TMEM columns of scales per stage
   static constexpr int kTmemCols = 512;
@@ -100,10 +107,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sfbuf + S * Cfg::kSfOps * kSfStageBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
-  uint64_t* acc_full = bars + 2 * S;
+  uint64_t* sf_ready = bars + 2 * S;
+  uint64_t* acc_full = bars + 3 * S;
   uint64_t* acc_empty = acc_full + Cfg::kAccBufs;
   uint64_t* drain = acc_empty + Cfg::kAccBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -114,12 +122,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&sf_ready[s], 1);
     }
     for (int b = 0; b < Cfg::kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 128);
     }
     mbar_init(drain, 1);
+    mbar_init(drain + 1, 1);
     fence_barrier_init();
     prefetch_tensormap(&tm_a);
     prefetch_tensormap(&tm_b);
@@ -195,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d0 = tmem_base + acc * Cfg::kAccCols;
         bool ok = true;
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&full[stage], phase)) {
+          if (!mbar_wait(&full[stage], phase) || !mbar_wait(&sf_ready[stage], phase)) {
             set_status(p.status, kStatusTimeoutFull);
             abort_flag = 1;
             ok = false;
@@ -203,23 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t st = smem_u32(tiles + stage * Cfg::kStageBytes);
-          const uint32_t sf = smem_u32(sfbuf + stage * Cfg::kSfOps * kSfStageBytes);
           const uint32_t sfc = tmem_base + sf_col0 + stage * Cfg::kSfCols;
-          // Scale blocks -> TMEM.  Per stage: SFA at columns [0,16) (MMA step kk
-          // at 4*kk), then per B operand 16*(BN/128) columns where the scales
-          // of 128-row block j for step kk sit at 4*(kk*(BN/128) + j), which is
-          // the column order an N=BN MMA reads them in.
-#pragma unroll
-          for (int kk = 0; kk < kBK / kMmaK; ++kk)
-            tmem_cp_32x128b_x4(sfc + 4 * kk, desc_sf_block(sf + kk * kSfBlockBytes));
-#pragma unroll
-          for (int op = 0; op < Cfg::kNB; ++op)
-#pragma unroll
-            for (int j = 0; j < BN / 128; ++j)
-#pragma unroll
-              for (int kk = 0; kk < kBK / kMmaK; ++kk)
-                tmem_cp_32x128b_x4(sfc + 16 + op * 16 * (BN / 128) + 4 * (kk * (BN / 128) + j),
-                                   desc_sf_block(sf + (1 + op * (BN / 128) + j) * kSfStageBytes + kk * kSfBlockBytes));
 #pragma unroll
           for (int kk = 0; kk < kBK / kMmaK; ++kk) {
             const uint64_t adesc = desc_kmajor_sw128(st + kk * (kMmaK / 2));
@@ -248,6 +242,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Make sure every issued tcgen05 op has retired before TMEM is freed.
       tc_commit(drain);
       mbar_wait(drain, 0);
+    }
+  } else if (warp == 6) {
+    // ------------------------------------------------------------ scale copier
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const int total = ((p.num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                         static_cast<int>(gridDim.x)) * KT;
+      for (int i = 0; i < total && !abort_flag; ++i) {
+        if (!mbar_wait(&full[stage], phase)) {
+          set_status(p.status, kStatusTimeoutFull);
+          abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sf = smem_u32(sfbuf + stage * Cfg::kSfOps * kSfStageBytes);
+        const uint32_t sfc = tmem_base + sf_col0 + stage * Cfg::kSfCols;
+        // Per stage: SFA at columns [0,16) (MMA step kk at 4*kk), then per B
+        // operand 16*(BN/128) columns where the scales of 128-row block j for
+        // step kk sit at 4*(kk*(BN/128) + j), the column order an N=BN MMA
+        // reads them in.
+#pragma unroll
+        for (int kk = 0; kk < kBK / kMmaK; ++kk)
+          tmem_cp_32x128b_x4(sfc + 4 * kk, desc_sf_block(sf + kk * kSfBlockBytes));
+#pragma unroll
+        for (int op = 0; op < Cfg::kNB; ++op)
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j)
+#pragma unroll
+            for (int kk = 0; kk < kBK / kMmaK; ++kk)
+              tmem_cp_32x128b_x4(sfc + 16 + op * 16 * (BN / 128) + 4 * (kk * (BN / 128) + j),
+                                 desc_sf_block(sf + (1 + op * (BN / 128) + j) * kSfStageBytes + kk * kSfBlockBytes));
+        tc_commit(&sf_ready[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      tc_commit(drain + 1);
+      mbar_wait(drain + 1, 0);
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -390,6 +424,13 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
 }
 
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {
+  static int forced_bn = -1;
+  if (forced_bn < 0) {
+    const char* e = getenv("NVFP4_GEMM_BN");
+    forced_bn = e ? atoi(e) : 0;
+  }
+  const bool wide = forced_bn ? forced_bn == 256 && g.N % 256 == 0 : g.N % 256 == 0;
+  if (wide) return launch_impl<256, false>(g, num_sms, stream, why);
   return launch_impl<128, false>(g, num_sms, stream, why);
 }
 
