@@ -45,6 +45,14 @@ CONFIGS = {
 }
 
 
+# committed ncu summaries (profiles/<name>.txt) of each workload's kernel
+PROFILE_NAMES = {
+    "gemv": "gemv_kernel_M7168_K16384_L4",
+    "gemm": "gemm_kernel_M1024_N7168_K16384",
+    "dual": "dual_gemm_kernel_M256_N4096_K7168",
+}
+
+
 def algo_bytes(problem, m, n, k, l):
     """Algorithmic bytes per call: packed operands, their scales and C (GEMV b unpadded)."""
     nb = 2 if problem == "dual" else 1
@@ -134,15 +142,6 @@ class ClockSampler:
         reasons = [v for b, v in self.REASONS.items() if mask & b and v != "gpu_idle"]
         return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": self.max_mhz,
                 "reasons": reasons, "samples": len(inside)}
-
-
-def shard_shape(cfg, world, rank):
-    m, n, k, l = cfg["m"], cfg["n"], cfg["k"], cfg["l"]
-    if cfg["shard"] == "m":
-        assert m % (128 * world) == 0
-        return m // world, n, k, l
-    assert n % (128 * world) == 0
-    return m, n // world, k, l
 
 
 def make_inputs(cfg, shape, seed, device):
@@ -285,18 +284,26 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
 
+    from nvfp4_b200 import shard
     problem = cfg["problem"]
     fn = kernel_fn(problem)
-    shape = shard_shape(cfg, world, rank)
-    m, n, k, l = shape
+    full_shape = (cfg["m"], cfg["n"], cfg["k"], cfg["l"])
+    # Every rank draws the full problem from the same seed and runs its shard
+    # (GEMV rows / GEMM columns) through views of it.
+    one_full = make_inputs(cfg, full_shape, 1111 + cfg["index"], dev)
+    one = shard.shard_tuple(problem, one_full, world, rank)
+    m, k2, l = one[0].shape
+    k = 2 * k2
+    n = 1 if problem == "gemv" else one[1].shape[0]
+    shape = (m, n, k, l)
     bytes_step = algo_bytes(problem, m, n, k, l)
     flops_step = algo_flops(problem, m, n, k, l)
 
     # Rotating input sets so that every step reads operands that are not in L2.
-    one = make_inputs(cfg, shape, 1111 + cfg["index"] + 1000 * rank, dev)
     read_bytes = sum(t.numel() * t.element_size() for t in used_tensors(problem, one)[0])
     nsets = max(1, min(8, math.ceil(2 * L2_BYTES / read_bytes) + (1 if read_bytes < L2_BYTES else 0)))
-    sets = [one] + [make_inputs(cfg, shape, 2000 + 17 * i + 1000 * rank, dev) for i in range(1, nsets)]
+    sets = [one] + [shard.shard_tuple(problem, make_inputs(cfg, full_shape, 2000 + 17 * i, dev), world, rank)
+                    for i in range(1, nsets)]
     torch.cuda.synchronize()
 
     stream = torch.cuda.current_stream(dev)
@@ -385,7 +392,7 @@ def main():
                 "frac": achieved / fp4_peak,
                 "peak_source": f"4 x {peak_kind} dense bf16 burst (B200 dense fp4 = 4x bf16)",
                 "frac_of_max_mem_fp4_roofline": (max(t_mem, t_fp4) * 1e3) / launch_ms}
-    roof["traffic"] = profile_traffic(f"{problem}_{cfg_name(cfg)}")
+    roof["traffic"] = profile_traffic(PROFILE_NAMES.get(cfg_name(cfg), "")) if world == 1 else None
     roof["kernel_ms_per_launch"] = launch_ms
     roof["algorithmic_bytes_per_launch"] = bytes_step
     if problem != "gemv":

@@ -1,0 +1,49 @@
+"""Splitting one problem across ranks (one process per GPU) without copies.
+
+The three problems shard with no exchange step: the GEMV by rows M, the GEMM
+and dual GEMM by columns N (B1 and B2 split identically so the SiLU gate stays
+element-local).  ``shard_tuple`` returns the rank's part of a reference input
+tuple as views (offset pointers and the full problem's strides), so the
+drop-in ``custom_kernel`` functions run on it unchanged and write straight into
+the rank's slice of C.  Shards are multiples of 128 rows / columns so that the
+128-row scale blocks are never split.
+"""
+from __future__ import annotations
+
+
+def shard_bounds(total: int, world: int, rank: int, align: int = 128) -> tuple[int, int]:
+    """[start, end) of `rank`'s part of `total` in units of `align`, as even as possible."""
+    assert total % align == 0, (total, align)
+    units = total // align
+    lo = (units * rank) // world
+    hi = (units * (rank + 1)) // world
+    return lo * align, hi * align
+
+
+def shard_tuple(problem: str, data, world: int, rank: int):
+    if world == 1:
+        return data
+    if problem == "gemv":
+        a, b, sfa, sfb, sfa_p, sfb_p, c = data
+        m0, m1 = shard_bounds(a.shape[0], world, rank)
+        return (a[m0:m1], b, sfa[m0:m1], sfb, sfa_p[:, :, m0 // 128:m1 // 128], sfb_p, c[m0:m1])
+    if problem == "gemm":
+        a, b, sfa, sfb, sfa_p, sfb_p, c = data
+        n0, n1 = shard_bounds(b.shape[0], world, rank)
+        return (a, b[n0:n1], sfa, sfb[n0:n1], sfa_p, sfb_p[:, :, n0 // 128:n1 // 128], c[:, n0:n1])
+    if problem == "dual":
+        a, b1, b2, sfa, sfb1, sfb2, sfa_p, sfb1_p, sfb2_p, c = data
+        n0, n1 = shard_bounds(b1.shape[0], world, rank)
+        blk = slice(n0 // 128, n1 // 128)
+        return (a, b1[n0:n1], b2[n0:n1], sfa, sfb1[n0:n1], sfb2[n0:n1], sfa_p,
+                sfb1_p[:, :, blk], sfb2_p[:, :, blk], c[:, n0:n1])
+    raise ValueError(problem)
+
+
+def output_slice(problem: str, shape, world: int, rank: int):
+    """Index expression of the rank's part of C ([M, N, L])."""
+    if problem == "gemv":
+        m0, m1 = shard_bounds(shape[0], world, rank)
+        return (slice(m0, m1), slice(None), slice(None))
+    n0, n1 = shard_bounds(shape[1], world, rank)
+    return (slice(None), slice(n0, n1), slice(None))
