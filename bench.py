@@ -160,8 +160,8 @@ def kernel_fn(problem):
 def used_tensors(problem, data):
     """The tuple members the kernel reads (copied host->device for e2e) and the output."""
     if problem == "gemv":
-        a, b, sfa, sfb, _, _, c = data
-        return [a, b, sfa, sfb], c
+        a, b, _, _, sfa_p, sfb_p, c = data
+        return [a, b, sfa_p, sfb_p], c
     if problem == "gemm":
         a, b, _, _, sfa_p, sfb_p, c = data
         return [a, b, sfa_p, sfb_p], c

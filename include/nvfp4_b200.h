@@ -25,7 +25,7 @@
  *   C               : fp16, row m of slice l at c + l*c_lstride + m*ldc
  *
  * All calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy
- * default stream) and allocate nothing.  Every entry point returns 0 on
+ * default stream); only nvfp4_gemv allocates (a workspace, once per device).  Every entry point returns 0 on
  * success or one of the NVFP4_ERR_* codes; nvfp4_last_error() then returns a
  * message (thread-local).  Nothing runs on the CPU: there is no fallback.
  */
@@ -59,14 +59,19 @@ int nvfp4_abi_version(void);
 int nvfp4_device_status(int clear);
 
 /* Batched GEMV: c[m, l] = fp16( sum_k a[m,k,l]*sfa[m,k/16,l] * b[0,k,l]*sfb[0,k/16,l] ).
- * Replaces the reference GEMV custom_kernel (nvfp4_gemv/submission.py:28-54).
- *   a   : packed [L][M][K/2]            a_lstride   (bytes, multiple of 16)
- *   b   : packed [L][rows>=1][K/2]      b_lstride   (bytes; the reference pads b to 128 rows)
- *   sfa : plain  [L][M][K/16]           sfa_lstride (bytes)
- *   sfb : plain  [L][rows>=1][K/16]     sfb_lstride (bytes)
- *   c   : fp16   [L][M]                 c_lstride   (elements)
- * Requires M % 4 == 0, K % 64 == 0 (the reference requires M % 128, K % 64). */
-int nvfp4_gemv(const void* a, const void* b, const void* sfa, const void* sfb, void* c, int M, int K, int L,
+ * Replaces the reference GEMV custom_kernel (nvfp4_gemv/submission.py:28-54;
+ * template_cute.py:199-247 reads the same blocked scales).
+ *   a       : packed [L][M][K/2]            a_lstride   (bytes, multiple of 16)
+ *   b       : packed [L][rows>=1][K/2]      b_lstride   (bytes; the reference pads b to 128 rows, row 0 is used)
+ *   sfa_blk : blocked scales of A           sfa_lstride (bytes, = M*K/16 for the reference tensors)
+ *   sfb_blk : blocked scales of b           sfb_lstride (bytes; 128-row block 0 is used)
+ *   c       : fp16 [L][M]                   c_lstride   (elements)
+ * Requires M % 128 == 0 and K % 64 == 0 (the reference's task.yml).  With
+ * K % 256 == 0 it runs the TMA + tensor-core kernel, which splits row blocks
+ * across SMs and uses a per-device workspace that the library allocates on the
+ * first call that needs it; GEMV calls on one device must not overlap on the
+ * GPU.  Other K use the SIMT kernel, which needs no workspace. */
+int nvfp4_gemv(const void* a, const void* b, const void* sfa_blk, const void* sfb_blk, void* c, int M, int K, int L,
                int64_t a_lstride, int64_t b_lstride, int64_t sfa_lstride, int64_t sfb_lstride, int64_t c_lstride,
                void* stream);
 

@@ -3,7 +3,9 @@
 // include/nvfp4_b200.h.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -49,6 +51,40 @@ static int num_sms_of(int dev) {
   return cache[dev];
 }
 
+// Per-device workspace for kernels that combine partial results across CTAs
+// (the tensor-core GEMV).  Allocated on the first call that needs it (and
+// grown when a later call needs more), zeroed once; the kernels leave it
+// zeroed.  Calls on one device share it, so they must not overlap on the GPU.
+struct DeviceWorkspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+static DeviceWorkspace g_ws[64];
+static std::mutex g_ws_mutex;
+
+static void* workspace_for(int dev, size_t bytes, cudaStream_t stream, cudaError_t* err) {
+  *err = cudaSuccess;
+  if (dev < 0 || dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  DeviceWorkspace& w = g_ws[dev];
+  if (w.bytes >= bytes) return w.ptr;
+  if (w.ptr) {
+    // earlier launches may still read the old buffer
+    if ((*err = cudaDeviceSynchronize()) != cudaSuccess) return nullptr;
+    cudaFree(w.ptr);
+    w.ptr = nullptr;
+    w.bytes = 0;
+  }
+  size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+  if ((*err = cudaMalloc(&w.ptr, want)) != cudaSuccess) return nullptr;
+  if ((*err = cudaMemsetAsync(w.ptr, 0, want, stream)) != cudaSuccess) return nullptr;
+  w.bytes = want;
+  return w.ptr;
+}
+
 static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 #define NVFP4_API extern "C" __attribute__((visibility("default")))
@@ -69,23 +105,52 @@ NVFP4_API int nvfp4_device_status(int clear) {
   return v;
 }
 
-NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa, const void* sfb, void* c, int M, int K, int L,
-               int64_t a_lstride, int64_t b_lstride, int64_t sfa_lstride, int64_t sfb_lstride, int64_t c_lstride,
-               void* stream) {
-  if (!a || !b || !sfa || !sfb || !c) return fail(NVFP4_ERR_NULL, "nvfp4_gemv: null pointer");
+NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa_blk, const void* sfb_blk, void* c, int M,
+                         int K, int L, int64_t a_lstride, int64_t b_lstride, int64_t sfa_lstride, int64_t sfb_lstride,
+                         int64_t c_lstride, void* stream) {
+  if (!a || !b || !sfa_blk || !sfb_blk || !c) return fail(NVFP4_ERR_NULL, "nvfp4_gemv: null pointer");
   if (M <= 0 || K <= 0 || L <= 0) return fail(NVFP4_ERR_SHAPE, "nvfp4_gemv: M, K, L must be positive");
-  if (M % 4 != 0) return fail(NVFP4_ERR_SHAPE, "nvfp4_gemv: M=%d must be a multiple of 4", M);
+  if (M % 128 != 0) return fail(NVFP4_ERR_SHAPE, "nvfp4_gemv: M=%d must be a multiple of 128", M);
   if (K % 64 != 0) return fail(NVFP4_ERR_SHAPE, "nvfp4_gemv: K=%d must be a multiple of 64", K);
-  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sfa, 2) || !aligned(sfb, 2) || !aligned(c, 2) ||
-      (a_lstride % 16) || (b_lstride % 16) || (sfa_lstride % 2) || (sfb_lstride % 2))
-    return fail(NVFP4_ERR_ALIGN, "nvfp4_gemv: a/b need 16-byte, scales 2-byte alignment (bases and batch strides)");
+  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sfa_blk, 16) || !aligned(sfb_blk, 16) || !aligned(c, 2) ||
+      (a_lstride % 16) || (b_lstride % 16) || (sfa_lstride % 16) || (sfb_lstride % 16))
+    return fail(NVFP4_ERR_ALIGN, "nvfp4_gemv: operands and scales need 16-byte aligned bases and batch strides");
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4_ERR_DEVICE, "nvfp4_gemv: no CUDA device");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const char* path = getenv("NVFP4_GEMV_PATH");
+  const bool simt = (K % 256 != 0) || (path && strcmp(path, "simt") == 0) ||
+                    gemv_tc_workspace_bytes(M, K, L, num_sms_of(dev)) == 0;
+  if (!simt) {
+    GemvTcArgs g{};
+    g.a = a;
+    g.b = b;
+    g.sfa = sfa_blk;
+    g.sfb = sfb_blk;
+    g.c = c;
+    g.M = M;
+    g.K = K;
+    g.L = L;
+    g.a_lstride = a_lstride;
+    g.b_lstride = b_lstride;
+    g.sfa_lstride = sfa_lstride;
+    g.sfb_lstride = sfb_lstride;
+    g.c_lstride = c_lstride;
+    g.workspace_bytes = gemv_tc_workspace_bytes(M, K, L, num_sms_of(dev));
+    cudaError_t e = cudaSuccess;
+    g.workspace = workspace_for(dev, g.workspace_bytes, s, &e);
+    if (!g.workspace) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: workspace: %s", cudaGetErrorString(e));
+    g.status = status_ptr(dev);
+    const char* why = nullptr;
+    e = launch_gemv_tc(g, num_sms_of(dev), s, &why);
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: %s", why ? why : cudaGetErrorString(e));
+    return NVFP4_OK;
+  }
   GemvParams p;
   p.a = static_cast<const uint8_t*>(a);
   p.b = static_cast<const uint8_t*>(b);
-  p.sfa = static_cast<const uint8_t*>(sfa);
-  p.sfb = static_cast<const uint8_t*>(sfb);
+  p.sfa = static_cast<const uint8_t*>(sfa_blk);
+  p.sfb = static_cast<const uint8_t*>(sfb_blk);
   p.c = static_cast<__half*>(c);
   p.M = M;
   p.K = K;
@@ -96,7 +161,7 @@ NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa, const vo
   p.sfb_lstride = sfb_lstride;
   p.c_lstride = c_lstride;
   p.ctas_per_l = 1;
-  cudaError_t e = launch_gemv(p, num_sms_of(dev), static_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_gemv(p, num_sms_of(dev), s);
   if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: launch failed: %s", cudaGetErrorString(e));
   return NVFP4_OK;
 }

@@ -361,14 +361,15 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 3-D byte tensor (K/2 inner, rows, L) with a (128 B x box_rows) box and 128-byte swizzle.
-static bool make_operand_map(CUtensorMap* map, const void* base, int K2, int rows, int L, int64_t lstride,
-                             int box_rows) {
+// 3-D byte tensor (inner bytes, rows, L) with a (box_inner x box_rows) box and
+// 128-byte swizzle; rows past `rows` read as zero.
+bool make_tma_3d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t L,
+                    uint64_t row_stride, uint64_t lstride, uint32_t box_inner, uint32_t box_rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(K2), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(L)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(K2), static_cast<cuuint64_t>(lstride)};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBKBytes), static_cast<cuuint32_t>(box_rows), 1};
+  cuuint64_t dims[3] = {inner, rows, L};
+  cuuint64_t strides[2] = {row_stride, lstride};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -376,7 +377,10 @@ static bool make_operand_map(CUtensorMap* map, const void* base, int K2, int row
   return r == CUDA_SUCCESS;
 }
 
-
+static bool make_operand_map(CUtensorMap* map, const void* base, int K2, int rows, int L, int64_t lstride,
+                             int box_rows) {
+  return make_tma_3d_u8(map, base, K2, rows, L, K2, lstride, kBKBytes, box_rows);
+}
 
 template <int BN, bool kDual>
 static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {

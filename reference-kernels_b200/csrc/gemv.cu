@@ -10,6 +10,8 @@
 //   * within a CTA the warps split K into 512-byte segments (one 16-byte
 //     ld.global.nc per lane per row) and every warp streams up to 8 rows at
 //     once, so each lane keeps eight 128-bit loads in flight;
+//   * scales are read from the 128x4-blocked layout (the same tensors the
+//     tensor-core path reads);
 //   * e2m1 pairs are widened with cvt.rn.f16x2.e2m1x2 and multiplied against
 //     the (unscaled) e2m1 values of b with HFMA2: the products of two e2m1
 //     values are multiples of 1/4 below 36, so the 8-term sums per f16 half
@@ -65,6 +67,13 @@ __device__ __forceinline__ float2 e4m3_pair(uint16_t codes) {
   return __half22float2(*reinterpret_cast<__half2*>(&h));
 }
 
+// Byte offset of scale (row i, group j) in the 128x4-blocked layout
+// (to_blocked of problems/nvidia/nvfp4_gemv/reference.py:14-25).  Groups 2t
+// and 2t+1 share one aligned 16-bit word.
+__device__ __forceinline__ int64_t blocked_offset(int i, int j, int sk) {
+  return static_cast<int64_t>(i >> 7) * (sk >> 2) * 512 + (j >> 2) * 512 + (i & 31) * 16 + ((i & 127) >> 5) * 4 + (j & 3);
+}
+
 // One work item = (batch of up to 8 rows, one 512-byte K segment of this warp).
 struct GemvItem {
   uint4 av[kGemvRowsPerBatch];
@@ -77,7 +86,7 @@ __device__ __forceinline__ void load_item(GemvItem& it, const uint8_t* a_l, cons
   for (int r = 0; r < kGemvRowsPerBatch; ++r) {
     if (r < nrows && kb < K2) {
       it.av[r] = ld_stream_16(a_l + static_cast<int64_t>(row0 + r) * K2 + kb);
-      it.sa[r] = __ldg(reinterpret_cast<const uint16_t*>(sfa_l + static_cast<int64_t>(row0 + r) * SK + (kb >> 3)));
+      it.sa[r] = __ldg(reinterpret_cast<const uint16_t*>(sfa_l + blocked_offset(row0 + r, kb >> 3, SK)));
     } else {
       it.av[r] = make_uint4(0, 0, 0, 0);
       it.sa[r] = 0;
@@ -157,7 +166,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvPara
 #pragma unroll
             for (int q = 0; q < 4; ++q) bh[i * 4 + q] = h[q];
           }
-          const float2 sb = e4m3_pair(*reinterpret_cast<const uint16_t*>(sfb_l + (kb >> 3)));
+          const float2 sb = e4m3_pair(*reinterpret_cast<const uint16_t*>(sfb_l + blocked_offset(0, kb >> 3, SK)));
           sb0 = sb.x;
           sb1 = sb.y;
           cached_seg = seg;

@@ -10,14 +10,31 @@ namespace nvfp4 {
 struct GemvParams {
   const uint8_t* a;    // [L][M][K/2] packed e2m1
   const uint8_t* b;    // [L][rows][K/2], row 0 used
-  const uint8_t* sfa;  // [L][M][K/16] e4m3 codes, plain layout
-  const uint8_t* sfb;  // [L][rows][K/16], row 0 used
+  const uint8_t* sfa;  // blocked (128x4) e4m3 scales of A, batch l at + l * sfa_lstride
+  const uint8_t* sfb;  // blocked scales of b (row block 0 used)
   __half* c;           // [L][M]
   int M, K, L;
   int64_t a_lstride, b_lstride, sfa_lstride, sfb_lstride, c_lstride;  // elements of each array
   int ctas_per_l;                                                      // set by the launcher
 };
 cudaError_t launch_gemv(const GemvParams& in, int num_sms, cudaStream_t stream);
+
+// GEMV through TMA + tcgen05 (gemv_tc.cu); blocked scales; M % 128 == 0, K % 256 == 0.
+struct GemvTcArgs {
+  const void *a, *b, *sfa, *sfb;
+  void* c;
+  int M, K, L;
+  int64_t a_lstride, b_lstride, sfa_lstride, sfb_lstride;  // bytes
+  int64_t c_lstride;                                        // elements
+  void* workspace;                                          // zero-initialised counters + partial sums
+  size_t workspace_bytes;
+  int* status;
+};
+// Row blocks (M/128 * L) the tensor-core GEMV can track; larger calls use the SIMT GEMV.
+constexpr int kGemvTcMaxCounterBlocks = 16384;
+// Bytes of workspace the tensor-core GEMV needs (0 if the call is too large for it).
+size_t gemv_tc_workspace_bytes(int M, int K, int L, int num_sms);
+cudaError_t launch_gemv_tc(const GemvTcArgs& g, int num_sms, cudaStream_t stream, const char** why);
 
 struct GemmArgs {
   const void *a, *b, *b2, *sfa, *sfb, *sfb2;

@@ -66,21 +66,19 @@ def _post():
 
 
 def gemv(data):
-    """custom_kernel for nvfp4_gemv: reads a, b, sfa, sfb (plain scales) and writes c[:, 0, :]."""
-    a, b, sfa, sfb, _sfa_p, _sfb_p, c = data
+    """custom_kernel for nvfp4_gemv: reads a, b and the blocked (permuted) scales, writes c[:, 0, :]."""
+    a, b, _sfa, _sfb, sfa_p, sfb_p, c = data
     m, k2, l = a.shape
     k = 2 * k2
     _check_operand(a, "a")
     _require(b.is_cuda and b.stride(1) == 1 and b.shape[1] == k2 and b.shape[2] == l, "b must be [rows, K/2, L]")
-    _require(sfa.stride(1) == 1 and sfa.stride(0) == k // 16 and tuple(sfa.shape) == (m, k // 16, l),
-             f"sfa must be plain [M, K/16, L] with unit inner stride (strides {sfa.stride()})")
-    _require(sfb.stride(1) == 1 and sfb.shape[1] == k // 16, "sfb must be plain [rows, K/16, L]")
     _require(c.dtype == torch.float16 and tuple(c.shape) == (m, 1, l), "c must be fp16 [M, 1, L]")
+    sa = _blocked_lstride(sfa_p, m, k // 16, "sfa_permuted")
+    sb = _blocked_lstride(sfb_p, sfb_p.shape[2] * 128 if sfb_p.dim() == 6 else 128, k // 16, "sfb_permuted")
     lib = _lib.load()
     _lib.check(lib.nvfp4_gemv(
-        a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), c.data_ptr(),
-        m, k, l, a.stride(2), b.stride(2), sfa.stride(2), sfb.stride(2), c.stride(2),
-        _stream_ptr(a)))
+        a.data_ptr(), b.data_ptr(), sfa_p.data_ptr(), sfb_p.data_ptr(), c.data_ptr(),
+        m, k, l, a.stride(2), b.stride(2), sa, sb, c.stride(2), _stream_ptr(a)))
     _post()
     return c
 

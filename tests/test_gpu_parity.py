@@ -32,8 +32,18 @@ DUAL_TESTS = [(1536, 512, 7168), (256, 512, 256), (3072, 1024, 1536), (7168, 102
               (4608, 384, 7168), (7168, 384, 2304), (512, 768, 7168), (4096, 768, 512)]
 
 
+@pytest.fixture(params=["tensorcore", "simt"])
+def gemv_path(request, monkeypatch):
+    """Both GEMV kernels: the TMA + tcgen05 one (default for K % 256 == 0) and the SIMT one."""
+    if request.param == "simt":
+        monkeypatch.setenv("NVFP4_GEMV_PATH", "simt")
+    else:
+        monkeypatch.delenv("NVFP4_GEMV_PATH", raising=False)
+    return request.param
+
+
 @pytest.mark.parametrize("m,k,l", GEMV_TESTS)
-def test_gemv_reference_tests(m, k, l):
+def test_gemv_reference_tests(m, k, l, gemv_path):
     data = inputs.reference_input("gemv", m, k, l, 1111)
     ref = scaled_mm_ref("gemv", data)
     out = run("gemv", data)
@@ -69,6 +79,18 @@ def test_against_oracle(dist, problem, m, n, k, l):
     exp = oracle_ref(problem, data)
     out = run(problem, data)
     assert_match(out, exp, f"{problem} {m}x{n}x{k}x{l} ({dist}) vs oracle")
+
+
+@pytest.mark.parametrize("m,k,l", [(7168, 16384, 4), (4096, 7168, 8), (7168, 2048, 4), (128, 1024, 1)])
+def test_gemv_benchmark_shapes_and_repeat(m, k, l, gemv_path):
+    """The reference's GEMV benchmark shapes (and configs[1]) on uniform inputs,
+    called twice: split row blocks are combined deterministically."""
+    data = inputs.baseline_input("gemv", m, k, l, 5)
+    ref = scaled_mm_ref("gemv", data)
+    o1 = run("gemv", data).clone()
+    o2 = run("gemv", data).clone()
+    assert torch.equal(o1, o2)
+    assert_match(o1, ref, f"gemv {m}x{k}x{l} vs _scaled_mm")
 
 
 def test_repeat_calls_identical():
