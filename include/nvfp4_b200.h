@@ -75,6 +75,30 @@ int nvfp4_gemv(const void* a, const void* b, const void* sfa_blk, const void* sf
                int64_t a_lstride, int64_t b_lstride, int64_t sfa_lstride, int64_t sfb_lstride, int64_t c_lstride,
                void* stream);
 
+/* nvfp4_gemv without any allocation.  No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory when they call the
+ * GEMV -- for example code whose memory is fully reserved up front by a pool
+ * or arena, or host code with no access to cudaMalloc -- and so cannot use
+ * nvfp4_gemv, whose tensor-core path allocates a workspace on first use.
+ * Same arguments, layouts and result as nvfp4_gemv; it runs the same
+ * tensor-core kernel with its scratch memory (arrival counters and partial
+ * sums) in a fixed array of NVFP4_GEMV_NOALLOC_SCRATCH_BYTES that the library
+ * holds on every GPU that loads it until the process exits.
+ *   - Requires M % 128 == 0 and K % 256 == 0; a shape whose scratch need
+ *     exceeds the array is rejected with NVFP4_ERR_SHAPE and a message.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - It calls no cudaMalloc / cudaFree; each call clears the counters with
+ *     cudaMemsetAsync on `stream`, then launches the kernel.
+ *   - All calls share the one array, which keeps the last call's contents:
+ *     calls that overlap on the GPU (other streams, other threads) race and
+ *     give wrong results. */
+#define NVFP4_GEMV_NOALLOC_SCRATCH_BYTES (4u << 20)
+int nvfp4_gemv_noalloc(const void* a, const void* b, const void* sfa_blk, const void* sfb_blk, void* c, int M, int K,
+                       int L, int64_t a_lstride, int64_t b_lstride, int64_t sfa_lstride, int64_t sfb_lstride,
+                       int64_t c_lstride, void* stream);
+
 /* Batched block-scaled GEMM: C = (A*sfA) (B*sfB)^T, fp32 accumulation, fp16 out.
  * Replaces nvfp4_gemm/submission.py:708-761.
  *   a       : packed [L][M][K/2]    a_lstride   (bytes)

@@ -25,6 +25,14 @@ static int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+int nvfp4_record_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
 // One device-resident status word per device; kernels record bounded-wait
 // timeouts here (0 = ok).
 static __device__ int g_status_word;

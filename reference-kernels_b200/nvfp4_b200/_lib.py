@@ -19,6 +19,7 @@ EXPORTS = (
     "nvfp4_gemv",
     "nvfp4_gemm",
     "nvfp4_dual_gemm",
+    "nvfp4_gemv_noalloc",
 )
 
 _P = ctypes.c_void_p
@@ -48,6 +49,8 @@ def load() -> ctypes.CDLL:
     lib.nvfp4_device_status.argtypes = [_I]
     lib.nvfp4_gemv.restype = _I
     lib.nvfp4_gemv.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _L, _P]
+    lib.nvfp4_gemv_noalloc.restype = _I
+    lib.nvfp4_gemv_noalloc.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _L, _P]
     lib.nvfp4_gemm.restype = _I
     lib.nvfp4_gemm.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _P]
     lib.nvfp4_dual_gemm.restype = _I
