@@ -25,7 +25,8 @@
  *   C               : fp16, row m of slice l at c + l*c_lstride + m*ldc
  *
  * All calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy
- * default stream); only nvfp4_gemv allocates (a workspace, once per device).  Every entry point returns 0 on
+ * default stream).  Only nvfp4_gemv (tensor-core path) uses a per-device
+ * workspace, which the library allocates on the first call that needs it.  Every entry point returns 0 on
  * success or one of the NVFP4_ERR_* codes; nvfp4_last_error() then returns a
  * message (thread-local).  Nothing runs on the CPU: there is no fallback.
  */

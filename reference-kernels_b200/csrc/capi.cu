@@ -222,6 +222,9 @@ NVFP4_API int nvfp4_gemm(const void* a, const void* b, const void* sfa_blk, cons
   g.ldc = ldc;
   g.c_lstride = c_lstride;
   g.status = status_ptr(dev);
+  const GemmPlan pl = gemm_plan(M, N, K, L, false, num_sms_of(dev));
+  g.bn = pl.bn;
+  g.splits = pl.splits;
   const char* why = nullptr;
   cudaError_t e = launch_gemm(g, num_sms_of(dev), static_cast<cudaStream_t>(stream), &why);
   if (e != cudaSuccess)
@@ -261,6 +264,9 @@ NVFP4_API int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, con
   g.ldc = ldc;
   g.c_lstride = c_lstride;
   g.status = status_ptr(dev);
+  const GemmPlan pl = gemm_plan(M, N, K, L, true, num_sms_of(dev));
+  g.bn = pl.bn;
+  g.splits = pl.splits;
   const char* why = nullptr;
   cudaError_t e = launch_dual_gemm(g, num_sms_of(dev), static_cast<cudaStream_t>(stream), &why);
   if (e != cudaSuccess)

@@ -31,6 +31,7 @@
 #include "kernels.h"
 
 #include <cstdlib>
+#include <mutex>
 
 namespace nvfp4 {
 
@@ -70,8 +71,34 @@ struct GemmParams {
   int64_t ldc, c_lstride;                          // elements
   int tiles_m, tiles_n, num_tiles;
   int group_m;  // raster: groups of group_m M-blocks sweep all N-blocks
+  int splits;   // K splits per tile (1 = none); work item = tile * splits + split.
+                // With splits > 1 the kernel is launched with clusters of
+                // `splits` CTAs, one item per CTA, cluster = tile.
+  int num_items;
   int* status;
 };
+
+// K-tile range [k0, k1) of split s.
+__device__ __forceinline__ void split_range(int KT, int splits, int s, int& k0, int& k1) {
+  k0 = (s * KT) / splits;
+  k1 = ((s + 1) * KT) / splits;
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// AND of `pred` over the 128 epilogue threads (named barrier 1).
+__device__ __forceinline__ bool epi_all(bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, 1, 128, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(pred))
+      : "memory");
+  return out != 0;
+}
 
 __device__ __forceinline__ void set_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
@@ -92,6 +119,57 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& mb,
 
 __device__ __forceinline__ float silu_mul(float x, float y) {
   return __fdividef(x, 1.0f + __expf(-x)) * y;
+}
+
+// 32 fp32 values -> fp16, four 16-byte stores.
+__device__ __forceinline__ void store_half_row32(__half* dst_row, const uint32_t (&r)[32]) {
+  uint4 out[4];
+  uint32_t* o = reinterpret_cast<uint32_t*>(out);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    __half2 h = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+    o[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(dst_row);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = out[i];
+}
+
+// For the four epilogue warps, the AND of `flag` over them (named barrier 1);
+// other warps get true without touching the barrier.
+__device__ __forceinline__ bool epi_all_maybe(bool is_epi, bool flag) {
+  return is_epi ? epi_all(flag) : true;
+}
+
+// Cluster-wide barrier (every thread of every CTA in the cluster), with
+// release/acquire ordering of shared::cluster accesses.
+__device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_peer(uint32_t saddr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// Column groups (32 output columns each) [g0, g1) owned by split rank s of S.
+__device__ __forceinline__ void share_groups(int ngroups, int S, int s, int& g0, int& g1) {
+  g0 = (s * ngroups) / S;
+  g1 = ((s + 1) * ngroups) / S;
 }
 
 template <int BN, bool kDual>
@@ -141,6 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t sf_col0 = Cfg::kAccBufs * Cfg::kAccCols;
+  bool split_ready = false;  // epilogue threads: this CTA's split partial is in TMEM
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -149,14 +228,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_b = policy_evict_first();
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < p.num_tiles && !abort_flag; t += gridDim.x) {
+      for (int it = blockIdx.x; it < p.num_items && !abort_flag; it += gridDim.x) {
+        const int t = it / p.splits;
+        int k0, k1;
+        split_range(KT, p.splits, it - t * p.splits, k0, k1);
         int mb, nb, l;
         tile_coords(p, t, mb, nb, l);
         const uint8_t* sfa_src = p.sfa + l * p.sfa_lstride + static_cast<int64_t>(mb) * p.K * 8;
         const uint8_t* sfb_src = p.sfb + l * p.sfb_lstride + static_cast<int64_t>(nb) * (BN / 128) * p.K * 8;
         const uint8_t* sfb2_src =
             kDual ? p.sfb2 + l * p.sfb2_lstride + static_cast<int64_t>(nb) * (BN / 128) * p.K * 8 : nullptr;
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = k0; kt < k1; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             set_status(p.status, kStatusTimeoutEmpty);
             abort_flag = 1;
@@ -195,7 +277,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = blockIdx.x; t < p.num_tiles && !abort_flag; t += gridDim.x) {
+      for (int it = blockIdx.x; it < p.num_items && !abort_flag; it += gridDim.x) {
+        int k0, k1;
+        split_range(KT, p.splits, it % p.splits, k0, k1);
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1)) {
           set_status(p.status, kStatusTimeoutAccEmpty);
           abort_flag = 1;
@@ -204,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d0 = tmem_base + acc * Cfg::kAccCols;
         bool ok = true;
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = k0; kt < k1; ++kt) {
           if (!mbar_wait(&full[stage], phase) || !mbar_wait(&sf_ready[stage], phase)) {
             set_status(p.status, kStatusTimeoutFull);
             abort_flag = 1;
@@ -218,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kBK / kMmaK; ++kk) {
             const uint64_t adesc = desc_kmajor_sw128(st + kk * (kMmaK / 2));
             const uint64_t bdesc = desc_kmajor_sw128(st + Cfg::kABytes + kk * (kMmaK / 2));
-            const uint32_t accum = (kt | kk) != 0;
+            const uint32_t accum = (kt != k0 || kk != 0) ? 1u : 0u;
             mma_nvf4(d0, adesc, bdesc, idesc, sfc + 4 * kk, sfc + 16 + 4 * kk * (BN / 128), accum);
             if (kDual) {
               const uint64_t b2desc = desc_kmajor_sw128(st + Cfg::kABytes + Cfg::kBBytes + kk * (kMmaK / 2));
@@ -248,8 +332,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      const int total = ((p.num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                         static_cast<int>(gridDim.x)) * KT;
+      int total = 0;
+      for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
+        int k0, k1;
+        split_range(KT, p.splits, it % p.splits, k0, k1);
+        total += k1 - k0;
+      }
       for (int i = 0; i < total && !abort_flag; ++i) {
         if (!mbar_wait(&full[stage], phase)) {
           set_status(p.status, kStatusTimeoutFull);
@@ -288,49 +376,146 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+    const bool split = p.splits > 1;
+    for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
+      const int t = it / p.splits;
       int mb, nb, l;
       tile_coords(p, t, mb, nb, l);
-      // All lanes must agree before the warp-collective tcgen05.ld below.
-      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase))) {
+      // All lanes (and, with split K, all four epilogue warps, which meet at
+      // named barriers below) must agree before the collective tcgen05.ld.
+      const bool got = mbar_wait(&acc_full[acc], acc_phase);
+      if (split ? !epi_all(got) : !__all_sync(0xffffffffu, got)) {
         if (lane == 0) set_status(p.status, kStatusTimeoutAccFull);
         abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const int row = mb * kBM + q * 32 + lane;
+      const int rloc = q * 32 + lane;
+      const int row = mb * kBM + rloc;
       __half* crow = p.c + l * p.c_lstride + static_cast<int64_t>(row) * p.ldc + static_cast<int64_t>(nb) * BN;
       const uint32_t tacc = tmem_base + acc * Cfg::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
+      if (!split) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tacc + c0, r);
-        if (kDual) {
-          uint32_t r2[32];
-          tmem_ld_32x32b_x32(tacc + BN + c0, r2);
-          tmem_wait_ld();
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tacc + c0, r);
+          if (kDual) {
+            uint32_t r2[32];
+            tmem_ld_32x32b_x32(tacc + BN + c0, r2);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            r[i] = __float_as_uint(silu_mul(__uint_as_float(r[i]), __uint_as_float(r2[i])));
-        } else {
-          tmem_wait_ld();
+            for (int i = 0; i < 32; ++i)
+              r[i] = __float_as_uint(silu_mul(__uint_as_float(r[i]), __uint_as_float(r2[i])));
+          } else {
+            tmem_wait_ld();
+          }
+          store_half_row32(crow + c0, r);
         }
-        uint4 out[4];
-        uint32_t* o = reinterpret_cast<uint32_t*>(out);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          __half2 h = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-          o[i] = *reinterpret_cast<uint32_t*>(&h);
-        }
-        uint4* dst = reinterpret_cast<uint4*>(crow + c0);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = out[i];
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+      } else {
+        // Split K: one item per CTA; the accumulator stays in TMEM for the
+        // cluster exchange below.
+        split_ready = true;
       }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
       if (++acc == Cfg::kAccBufs) {
         acc = 0;
         acc_phase ^= 1;
+      }
+    }
+  }
+
+  if (p.splits > 1) {
+    // ---------------------------------------------------------- split-K reduction
+    // The CTAs of a cluster hold the partial sums of one tile for different K
+    // ranges.  Columns are cut into S shares (groups of 32 output columns, with
+    // both accumulators of a group for the dual GEMM); rank r writes its
+    // partials of every other rank's share straight into that rank's shared
+    // memory (st.shared::cluster), then each rank adds the partials of its own
+    // share in rank order (identical on every call) and writes C.  The
+    // pipeline shared memory is reused as the receive buffer, so the first
+    // cluster barrier waits until every rank's main loop is done with it.
+    constexpr int NG = BN / 32;
+    constexpr int GF = 32 * Cfg::kNB;  // floats per row per group
+    const int S = p.splits;
+    const int rank = static_cast<int>(cluster_ctarank());
+    const int t = blockIdx.x / S;
+    const int max_share = (NG + S - 1) / S;
+    const bool epi = warp >= 2 && warp <= 5;
+    const bool ok = epi_all_maybe(epi, split_ready);
+    tc_fence_after();
+    cluster_sync_all();  // every rank: main loop finished, smem free
+    const int q = warp & 3;
+    const int rloc = q * 32 + lane;
+    const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    // recv[slot][group][f4][row][4 floats], slot = sender rank minus one if above us
+    auto recv_off = [&](int slot, int gi, int f4) -> uint32_t {
+      return static_cast<uint32_t>((((slot * max_share + gi) * (GF / 4) + f4) * kBM + rloc) * 16);
+    };
+    if (epi && ok) {
+      const uint32_t base = smem_u32(tiles);
+      for (int peer = 0; peer < S; ++peer) {
+        if (peer == rank) continue;
+        const uint32_t pbase = map_peer(base, static_cast<uint32_t>(peer));
+        const int slot = rank < peer ? rank : rank - 1;
+        int g0, g1;
+        share_groups(NG, S, peer, g0, g1);
+        for (int g = g0; g < g1; ++g) {
+#pragma unroll
+          for (int b = 0; b < Cfg::kNB; ++b) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tacc + b * BN + g * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              st_cluster_v4(pbase + recv_off(slot, g - g0, b * 8 + i), __uint_as_float(r[4 * i]),
+                            __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
+                            __uint_as_float(r[4 * i + 3]));
+          }
+        }
+      }
+    }
+    cluster_sync_all();  // all partials delivered
+    if (epi && ok) {
+      int mb, nb, l;
+      tile_coords(p, t, mb, nb, l);
+      const int row = mb * kBM + rloc;
+      __half* crow = p.c + l * p.c_lstride + static_cast<int64_t>(row) * p.ldc + static_cast<int64_t>(nb) * BN;
+      int g0, g1;
+      share_groups(NG, S, rank, g0, g1);
+      const float4* recv = reinterpret_cast<const float4*>(tiles);
+      for (int g = g0; g < g1; ++g) {
+        // Own partial first, then the received ones in slot (rank) order:
+        // the same rank owns the same columns on every call, so the order of
+        // the additions, and the result, is the same on every call.
+        float acc[Cfg::kNB][32];
+#pragma unroll
+        for (int b = 0; b < Cfg::kNB; ++b) {
+          uint32_t own[32];
+          tmem_ld_32x32b_x32(tacc + b * BN + g * 32, own);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[b][i] = __uint_as_float(own[i]);
+        }
+        const float4* src = recv + ((g - g0) * (GF / 4)) * kBM + rloc;
+        for (int slot = 0; slot < S - 1; ++slot, src += max_share * (GF / 4) * kBM) {
+#pragma unroll
+          for (int b = 0; b < Cfg::kNB; ++b) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 v = src[(b * 8 + i) * kBM];
+              acc[b][4 * i] += v.x;
+              acc[b][4 * i + 1] += v.y;
+              acc[b][4 * i + 2] += v.z;
+              acc[b][4 * i + 3] += v.w;
+            }
+          }
+        }
+        uint32_t res[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          res[i] = __float_as_uint(kDual ? silu_mul(acc[0][i], acc[Cfg::kNB - 1][i]) : acc[0][i]);
+        store_half_row32(crow + g * 32, res);
       }
     }
   }
@@ -363,8 +548,49 @@ static EncodeTiledFn get_encode_fn() {
 
 // 3-D byte tensor (inner bytes, rows, L) with a (box_inner x box_rows) box and
 // 128-byte swizzle; rows past `rows` read as zero.
+// Encoded tensor maps are cached (direct-mapped on the full argument tuple):
+// encoding costs microseconds of host time per map, and callers typically
+// reuse the same buffers call after call.
+namespace {
+struct TmaKey {
+  const void* base;
+  uint64_t inner, rows, L, row_stride, lstride;
+  uint32_t box_inner, box_rows;
+  bool operator==(const TmaKey& o) const {
+    return base == o.base && inner == o.inner && rows == o.rows && L == o.L && row_stride == o.row_stride &&
+           lstride == o.lstride && box_inner == o.box_inner && box_rows == o.box_rows;
+  }
+};
+struct TmaEntry {
+  TmaKey key;
+  CUtensorMap map;
+  bool valid;
+};
+constexpr int kTmaCacheSize = 1024;
+TmaEntry g_tma_cache[kTmaCacheSize];
+std::mutex g_tma_mutex;
+
+size_t tma_hash(const TmaKey& k) {
+  uint64_t h = reinterpret_cast<uint64_t>(k.base) * 0x9E3779B97F4A7C15ull;
+  for (uint64_t v : {k.inner, k.rows, k.L, k.row_stride, k.lstride, uint64_t(k.box_inner) << 32 | k.box_rows})
+    h = (h ^ v) * 0xBF58476D1CE4E5B9ull;
+  return static_cast<size_t>(h >> 40) % kTmaCacheSize;
+}
+}  // namespace
+
+// 3-D byte tensor (inner bytes, rows, L) with a (box_inner x box_rows) box and
+// 128-byte swizzle; rows past `rows` read as zero.
 bool make_tma_3d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t L,
                     uint64_t row_stride, uint64_t lstride, uint32_t box_inner, uint32_t box_rows) {
+  const TmaKey key{base, inner, rows, L, row_stride, lstride, box_inner, box_rows};
+  const size_t slot = tma_hash(key);
+  {
+    std::lock_guard<std::mutex> lock(g_tma_mutex);
+    if (g_tma_cache[slot].valid && g_tma_cache[slot].key == key) {
+      *map = g_tma_cache[slot].map;
+      return true;
+    }
+  }
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[3] = {inner, rows, L};
@@ -374,7 +600,12 @@ bool make_tma_3d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> lock(g_tma_mutex);
+  g_tma_cache[slot].key = key;
+  g_tma_cache[slot].map = *map;
+  g_tma_cache[slot].valid = true;
+  return true;
 }
 
 static bool make_operand_map(CUtensorMap* map, const void* base, int K2, int rows, int L, int64_t lstride,
@@ -422,19 +653,60 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
   p.num_tiles = p.tiles_m * p.tiles_n * g.L;
   p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
   p.status = g.status;
-  const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
-  gemm_kernel<BN, kDual><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tb2, p);
-  return cudaGetLastError();
+  p.splits = g.splits > 1 ? g.splits : 1;
+  p.num_items = p.num_tiles * p.splits;
+  if (p.splits == 1) {
+    const int grid = p.num_items < num_sms ? p.num_items : num_sms;
+    gemm_kernel<BN, kDual><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tb2, p);
+    return cudaGetLastError();
+  }
+  // Split K: one CTA per (tile, split), the splits of a tile in one cluster.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.num_items, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, kDual>, ta, tb, tb2, p);
+}
+
+static int env_int(const char* name) {
+  const char* e = getenv(name);
+  return e ? atoi(e) : 0;
+}
+
+// Tile width and K splits for a problem.  Problems with fewer tiles than SMs
+// (the dual GEMM's M=256 shapes, M=128 GEMMs) split K so more SMs work; the
+// splits of a tile form one thread-block cluster and are reduced on chip.
+// NVFP4_GEMM_BN / NVFP4_SPLITS override the choice (tuning only).
+GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms) {
+  GemmPlan pl;
+  const int forced_bn = env_int("NVFP4_GEMM_BN");
+  pl.bn = (!dual && N % 256 == 0 && forced_bn != 128) ? 256 : 128;
+  const int tiles = (M / 128) * (N / pl.bn) * L;
+  const int KT = K / 256;
+  const int ngroups = pl.bn / 32;  // a split owns at least one 32-column group of the tile
+  int splits = 1;
+  if (tiles < num_sms) splits = num_sms / tiles;
+  const int forced = env_int("NVFP4_SPLITS");
+  if (forced > 0) splits = forced;
+  if (splits > KT / 2) splits = KT / 2;  // at least two K tiles per split
+  if (splits > ngroups) splits = ngroups;
+  if (splits > 8) splits = 8;            // portable cluster size
+  if (tiles * splits > num_sms) splits = num_sms / tiles;
+  pl.splits = splits < 1 ? 1 : splits;
+  pl.workspace_bytes = 0;
+  return pl;
 }
 
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {
-  static int forced_bn = -1;
-  if (forced_bn < 0) {
-    const char* e = getenv("NVFP4_GEMM_BN");
-    forced_bn = e ? atoi(e) : 0;
-  }
-  const bool wide = forced_bn ? forced_bn == 256 && g.N % 256 == 0 : g.N % 256 == 0;
-  if (wide) return launch_impl<256, false>(g, num_sms, stream, why);
+  if (g.bn == 256) return launch_impl<256, false>(g, num_sms, stream, why);
   return launch_impl<128, false>(g, num_sms, stream, why);
 }
 

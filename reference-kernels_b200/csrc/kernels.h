@@ -44,7 +44,14 @@ struct GemmArgs {
   int64_t sfa_lstride, sfb_lstride, sfb2_lstride;  // bytes
   int64_t ldc, c_lstride;                          // elements
   int* status;                                     // device status word (bounded-wait timeouts)
+  int bn, splits;                                  // from gemm_plan
 };
+struct GemmPlan {
+  int bn;      // N tile: 128 or 256
+  int splits;  // K splits per tile
+  size_t workspace_bytes;  // always 0 (split K reduces on chip)
+};
+GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms);
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why);
 cudaError_t launch_dual_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why);
 

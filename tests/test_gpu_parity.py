@@ -118,3 +118,26 @@ def test_non_contiguous_output_shard():
     torch.cuda.synchronize()
     assert torch.equal(out[:, n0:n1], full[:, n0:n1])
     assert torch.count_nonzero(out[:, :n0]) == 0 and torch.count_nonzero(out[:, n1:]) == 0
+
+
+@pytest.mark.parametrize("splits", [2, 3, 5])
+@pytest.mark.parametrize("problem,m,n,k", [("gemm", 256, 512, 2816), ("dual", 256, 384, 2816), ("gemm", 128, 256, 1280)])
+def test_split_k_matches_oracle_and_repeats(problem, m, n, k, splits, monkeypatch):
+    """Split-K tiles (partials combined in split order by the last arriver):
+    parity with the CPU oracle and bit-identical repeated calls."""
+    monkeypatch.setenv("NVFP4_SPLITS", str(splits))
+    data = inputs.baseline_input(problem, m, k, 1, 9, n=n)
+    exp = oracle_ref(problem, data)
+    o1 = run(problem, data).clone()
+    o2 = run(problem, data).clone()
+    assert torch.equal(o1, o2)
+    assert_match(o1, exp, f"{problem} {m}x{n}x{k} splits={splits}")
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 4096, 7168), (512, 4096, 7168), (256, 3072, 4096), (512, 3072, 7168)])
+def test_dual_benchmark_shapes(m, n, k):
+    """The reference's dual-GEMM benchmark shapes (split K) against _scaled_mm."""
+    data = inputs.reference_input("dual", m, k, 1, 1111, n=n)
+    ref = scaled_mm_ref("dual", data)
+    out = run("dual", data)
+    assert_match(out, ref, f"dual {m}x{n}x{k} vs _scaled_mm")
