@@ -5,18 +5,19 @@
 //   Dual:  C[m,n,l] = fp16( silu(A.B1^T) * (A.B2^T) ), both products in fp32
 //          ref_kernel of problems/nvidia/nvfp4_dual_gemm/reference.py:27-77
 //
-// Structure (one CTA per SM, persistent, 7 warps):
+// Structure (one CTA per SM, persistent, 8 warps):
 //   warp 0      TMA producer: A/B tiles with 128-byte swizzle through
 //               cp.async.bulk.tensor, the 128x4-blocked scale factors through
 //               plain cp.async.bulk (each 128-row block of scales for a
 //               256-wide K tile is one contiguous 2 KB run), into a ring of
 //               kStages shared-memory stages guarded by full/empty mbarriers.
-//   warp 6      scale copier: per K tile, tcgen05.cp moves the stage's scale
+//   warps 6, 7  scale copiers: per K tile, tcgen05.cp moves the stage's scale
 //               blocks into TMEM (32x128b, replicated to the four lane
-//               quarters) and commits to sf_ready[stage].  Copies issued by
-//               the MMA thread itself would serialise with its MMAs in the
-//               tensor pipe (measured ~45 cycles per copy); from a second
-//               thread they overlap with the MMAs.
+//               quarters), the copies split between the two warps, which then
+//               commit to sf_ready[stage].  Copies issued by the MMA thread
+//               itself serialise with its MMAs (measured ~45 tensor-pipe
+//               cycles per copy); issued from other threads they overlap, and
+//               two copier threads beat one (measured; four are slower).
 //   warp 1      TMEM owner and MMA issuer: per K tile, four tcgen05.mma
 //               kind::mxf4nvf4 (M=128, N=BN, K=64 each; two per step for the
 //               dual GEMM, sharing the A tile) accumulate in fp32 in TMEM;
@@ -41,7 +42,8 @@ constexpr int kBKBytes = kBK / 2;
 constexpr int kMmaK = 64;         // K per tcgen05.mma for kind::mxf4nvf4
 constexpr int kSfBlockBytes = 512;  // one 128-row x 4-scale block
 constexpr int kSfStageBytes = kSfBlockBytes * (kBK / kMmaK);  // 2 KB per operand per stage
-constexpr int kThreads = 224;
+constexpr int kCopiers = 2;  // scale-copier warps (6, 7)
+constexpr int kThreads = 192 + 32 * kCopiers;
 
 template <int BN, bool kDual>
 struct GemmConfig {
@@ -189,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = bars + 3 * S;
   uint64_t* acc_empty = acc_full + Cfg::kAccBufs;
   uint64_t* drain = acc_empty + Cfg::kAccBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1 + kCopiers);
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -200,14 +202,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&sf_ready[s], 1);
+      mbar_init(&sf_ready[s], kCopiers);
     }
     for (int b = 0; b < Cfg::kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 128);
     }
-    mbar_init(drain, 1);
-    mbar_init(drain + 1, 1);
+    for (int d = 0; d <= kCopiers; ++d) mbar_init(drain + d, 1);
     fence_barrier_init();
     prefetch_tensormap(&tm_a);
     prefetch_tensormap(&tm_b);
@@ -327,8 +328,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(drain);
       mbar_wait(drain, 0);
     }
-  } else if (warp == 6) {
-    // ------------------------------------------------------------ scale copier
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------ scale copiers
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
@@ -351,25 +352,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         // operand 16*(BN/128) columns where the scales of 128-row block j for
         // step kk sit at 4*(kk*(BN/128) + j), the column order an N=BN MMA
         // reads them in.
+        // The copies of a stage are dealt round-robin to the copier warps,
+        // which issue them in parallel; sf_ready completes after all commit.
+        const int ci = warp - 6;
 #pragma unroll
         for (int kk = 0; kk < kBK / kMmaK; ++kk)
-          tmem_cp_32x128b_x4(sfc + 4 * kk, desc_sf_block(sf + kk * kSfBlockBytes));
+          if (kk % kCopiers == ci) tmem_cp_32x128b_x4(sfc + 4 * kk, desc_sf_block(sf + kk * kSfBlockBytes));
 #pragma unroll
         for (int op = 0; op < Cfg::kNB; ++op)
 #pragma unroll
           for (int j = 0; j < BN / 128; ++j)
 #pragma unroll
             for (int kk = 0; kk < kBK / kMmaK; ++kk)
-              tmem_cp_32x128b_x4(sfc + 16 + op * 16 * (BN / 128) + 4 * (kk * (BN / 128) + j),
-                                 desc_sf_block(sf + (1 + op * (BN / 128) + j) * kSfStageBytes + kk * kSfBlockBytes));
+              if ((kBK / kMmaK + (op * (BN / 128) + j) * (kBK / kMmaK) + kk) % kCopiers == ci)
+                tmem_cp_32x128b_x4(sfc + 16 + op * 16 * (BN / 128) + 4 * (kk * (BN / 128) + j),
+                                   desc_sf_block(sf + (1 + op * (BN / 128) + j) * kSfStageBytes + kk * kSfBlockBytes));
         tc_commit(&sf_ready[stage]);
         if (++stage == S) {
           stage = 0;
           phase ^= 1;
         }
       }
-      tc_commit(drain + 1);
-      mbar_wait(drain + 1, 0);
+      tc_commit(drain + 1 + (warp - 6));
+      mbar_wait(drain + 1 + (warp - 6), 0);
     }
   } else {
     // ------------------------------------------------------------ epilogue
