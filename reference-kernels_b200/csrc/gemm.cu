@@ -559,11 +559,16 @@ static EncodeTiledFn get_encode_fn() {
 namespace {
 struct TmaKey {
   const void* base;
-  uint64_t inner, rows, L, row_stride, lstride;
-  uint32_t box_inner, box_rows;
+  int rank;
+  uint64_t dims[4], strides[3];
+  uint32_t box[4];
   bool operator==(const TmaKey& o) const {
-    return base == o.base && inner == o.inner && rows == o.rows && L == o.L && row_stride == o.row_stride &&
-           lstride == o.lstride && box_inner == o.box_inner && box_rows == o.box_rows;
+    if (base != o.base || rank != o.rank) return false;
+    for (int i = 0; i < 4; ++i)
+      if (dims[i] != o.dims[i] || box[i] != o.box[i]) return false;
+    for (int i = 0; i < 3; ++i)
+      if (strides[i] != o.strides[i]) return false;
+    return true;
   }
 };
 struct TmaEntry {
@@ -576,18 +581,27 @@ TmaEntry g_tma_cache[kTmaCacheSize];
 std::mutex g_tma_mutex;
 
 size_t tma_hash(const TmaKey& k) {
-  uint64_t h = reinterpret_cast<uint64_t>(k.base) * 0x9E3779B97F4A7C15ull;
-  for (uint64_t v : {k.inner, k.rows, k.L, k.row_stride, k.lstride, uint64_t(k.box_inner) << 32 | k.box_rows})
-    h = (h ^ v) * 0xBF58476D1CE4E5B9ull;
+  uint64_t h = reinterpret_cast<uint64_t>(k.base) * 0x9E3779B97F4A7C15ull + k.rank;
+  for (int i = 0; i < 4; ++i) h = (h ^ k.dims[i] ^ (uint64_t(k.box[i]) << 40)) * 0xBF58476D1CE4E5B9ull;
+  for (int i = 0; i < 3; ++i) h = (h ^ k.strides[i]) * 0x94D049BB133111EBull;
   return static_cast<size_t>(h >> 40) % kTmaCacheSize;
 }
 }  // namespace
 
-// 3-D byte tensor (inner bytes, rows, L) with a (box_inner x box_rows) box and
-// 128-byte swizzle; rows past `rows` read as zero.
-bool make_tma_3d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t L,
-                    uint64_t row_stride, uint64_t lstride, uint32_t box_inner, uint32_t box_rows) {
-  const TmaKey key{base, inner, rows, L, row_stride, lstride, box_inner, box_rows};
+// Byte tensor of rank 3 or 4 (dims[0] innermost, strides in bytes for dims
+// 1..rank-1) with a box of `box` and 128-byte swizzle; out-of-range rows read
+// as zero.  Encoded maps are cached (direct-mapped on the full argument set):
+// encoding costs microseconds of host time, and callers reuse buffers.
+bool make_tma_u8(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                 const uint32_t* box) {
+  TmaKey key{};
+  key.base = base;
+  key.rank = rank;
+  for (int i = 0; i < rank; ++i) {
+    key.dims[i] = dims[i];
+    key.box[i] = box[i];
+    if (i > 0) key.strides[i - 1] = strides[i - 1];
+  }
   const size_t slot = tma_hash(key);
   {
     std::lock_guard<std::mutex> lock(g_tma_mutex);
@@ -598,11 +612,14 @@ bool make_tma_3d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
   }
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
-  cuuint64_t dims[3] = {inner, rows, L};
-  cuuint64_t strides[2] = {row_stride, lstride};
-  cuuint32_t box[3] = {box_inner, box_rows, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+  cuuint64_t d[4], st[3];
+  cuuint32_t bx[4], es[4] = {1, 1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    if (i > 0) st[i - 1] = strides[i - 1];
+  }
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), d, st, bx, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
@@ -611,6 +628,14 @@ bool make_tma_3d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
   g_tma_cache[slot].map = *map;
   g_tma_cache[slot].valid = true;
   return true;
+}
+
+bool make_tma_3d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t L,
+                    uint64_t row_stride, uint64_t lstride, uint32_t box_inner, uint32_t box_rows) {
+  const uint64_t dims[3] = {inner, rows, L};
+  const uint64_t strides[2] = {row_stride, lstride};
+  const uint32_t box[3] = {box_inner, box_rows, 1};
+  return make_tma_u8(map, base, 3, dims, strides, box);
 }
 
 static bool make_operand_map(CUtensorMap* map, const void* base, int K2, int rows, int L, int64_t lstride,

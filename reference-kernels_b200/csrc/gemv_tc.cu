@@ -11,7 +11,7 @@
 // multiply-accumulate in TMEM: B is b's row 0 in a 32-row tile whose other
 // rows are TMA zero fill, and only column 0 of the accumulator is read.
 //
-// Work split: the (l, 128-row block, 256-wide K tile) units are cut into one
+// Work split: the (l, 128-row block, 256- or 512-wide K range) units are cut into one
 // contiguous range per CTA (one CTA per SM), so every SM streams the same
 // number of bytes.  A CTA accumulates each run of units of one row block in
 // TMEM; a block whose K range is split over several CTAs is finished by the
@@ -30,21 +30,30 @@ namespace gemvtc {
 
 constexpr int kBM = 128;
 constexpr int kBN = 32;         // MMA N; only row 0 of B is real
-constexpr int kBK = 256;        // K elements per unit (128 bytes of a row)
+constexpr int kBK = 256;        // K elements per sub-tile (128 bytes of a row)
 constexpr int kBKBytes = kBK / 2;
-constexpr int kStages = 8;
-constexpr int kABytes = kBM * kBKBytes;  // 16 KB
-constexpr int kBBytes = kBN * kBKBytes;  // 4 KB
-constexpr int kSfBytes = 2048;           // one 128-row scale block for 4 MMA steps
-constexpr int kStageBytes = kABytes + kBBytes + 2 * kSfBytes;
-constexpr int kTxBytes = kStageBytes;
+constexpr int kASub = kBM * kBKBytes;  // 16 KB
+constexpr int kBSub = kBN * kBKBytes;  // 4 KB
+constexpr int kSfSub = 2048;           // one 128-row scale block for 4 MMA steps
 constexpr int kAccCols = kBN;
 constexpr int kAccBufs = 2;
-constexpr int kSfCols = 32;  // SFA 16 + SFB 16 per stage
 constexpr int kTmemCols = 512;
-static_assert(kAccBufs * kAccCols + kStages * kSfCols <= kTmemCols, "TMEM budget");
-constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
 constexpr int kThreads = 224;
+
+// A unit is SUB consecutive 256-wide K sub-tiles of one 128-row block; one
+// stage holds one unit and is filled by one TMA request per operand (a box
+// of SUB 128-byte columns), so wider units mean fewer, larger requests.
+template <int SUB>
+struct Cfg {
+  static constexpr int kStages = SUB == 1 ? 8 : 4;
+  static constexpr int kA = SUB * kASub;
+  static constexpr int kB = SUB * kBSub;
+  static constexpr int kSf = SUB * kSfSub;
+  static constexpr int kStageBytes = kA + kB + 2 * kSf;
+  static constexpr int kSfCols = 32 * SUB;  // per stage: SFA 16 + SFB 16 per sub-tile
+  static_assert(kAccBufs * kAccCols + kStages * kSfCols <= kTmemCols, "TMEM budget");
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+};
 
 }  // namespace gemvtc
 
@@ -93,10 +102,16 @@ __device__ __forceinline__ bool epi_all(bool pred) {
   return out != 0;
 }
 
+template <int SUB>
 __global__ void __launch_bounds__(gemvtc::kThreads, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const GemvTcParams p) {
   using namespace gemvtc;
+  using C = Cfg<SUB>;
+  constexpr int kStages = C::kStages;
+  constexpr int kStageBytes = C::kStageBytes;
+  constexpr int kSfCols = C::kSfCols;
+  constexpr int kTxBytes = kStageBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -156,13 +171,13 @@ __global__ void __launch_bounds__(gemvtc::kThreads, 1)
         }
         uint8_t* st = smem + stage * kStageBytes;
         mbar_arrive_expect_tx(&full[stage], kTxBytes);
-        tma_load_3d(st, &tm_a, &full[stage], kt * kBKBytes, mb * kBM, l, pol_stream);
-        tma_load_3d(st + kABytes, &tm_b, &full[stage], kt * kBKBytes, 0, l, pol_keep);
-        bulk_load(st + kABytes + kBBytes,
-                  p.sfa + l * p.sfa_lstride + static_cast<int64_t>(mb) * p.K * 8 + kt * kSfBytes, kSfBytes,
+        tma_load_4d(st, &tm_a, &full[stage], 0, mb * kBM, kt * SUB, l, pol_stream);
+        tma_load_4d(st + C::kA, &tm_b, &full[stage], 0, 0, kt * SUB, l, pol_keep);
+        bulk_load(st + C::kA + C::kB,
+                  p.sfa + l * p.sfa_lstride + static_cast<int64_t>(mb) * p.K * 8 + kt * C::kSf, C::kSf,
                   &full[stage], pol_stream);
-        bulk_load(st + kABytes + kBBytes + kSfBytes, p.sfb + l * p.sfb_lstride + kt * kSfBytes, kSfBytes,
-                  &full[stage], pol_keep);
+        bulk_load(st + C::kA + C::kB + C::kSf, p.sfb + l * p.sfb_lstride + kt * C::kSf, C::kSf, &full[stage],
+                  pol_keep);
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1;
@@ -181,13 +196,15 @@ __global__ void __launch_bounds__(gemvtc::kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t sf = smem_u32(smem + stage * kStageBytes + kABytes + kBBytes);
+        const uint32_t sf = smem_u32(smem + stage * kStageBytes + C::kA + C::kB);
         const uint32_t sfc = tmem_base + sf_col0 + stage * kSfCols;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          tmem_cp_32x128b_x4(sfc + 4 * kk, desc_sf_block(sf + kk * 512));
-          tmem_cp_32x128b_x4(sfc + 16 + 4 * kk, desc_sf_block(sf + kSfBytes + kk * 512));
-        }
+        for (int j = 0; j < SUB; ++j)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            tmem_cp_32x128b_x4(sfc + 32 * j + 4 * kk, desc_sf_block(sf + j * kSfSub + kk * 512));
+            tmem_cp_32x128b_x4(sfc + 32 * j + 16 + 4 * kk, desc_sf_block(sf + C::kSf + j * kSfSub + kk * 512));
+          }
         tc_commit(&sf_ready[stage]);
         if (++stage == kStages) {
           stage = 0;
@@ -225,9 +242,11 @@ __global__ void __launch_bounds__(gemvtc::kThreads, 1)
         const uint32_t sfc = tmem_base + sf_col0 + stage * kSfCols;
         const uint32_t d = tmem_base + acc * kAccCols;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_nvf4(d, desc_kmajor_sw128(st + kk * 32), desc_kmajor_sw128(st + kABytes + kk * 32), idesc, sfc + 4 * kk,
-                   sfc + 16 + 4 * kk, (seg_begin && kk == 0) ? 0u : 1u);
+        for (int j = 0; j < SUB; ++j)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_nvf4(d, desc_kmajor_sw128(st + j * kASub + kk * 32), desc_kmajor_sw128(st + C::kA + j * kBSub + kk * 32),
+                     idesc, sfc + 32 * j + 4 * kk, sfc + 32 * j + 16 + 4 * kk, (seg_begin && j == 0 && kk == 0) ? 0u : 1u);
         tc_commit(&empty[stage]);
         if (++stage == kStages) {
           stage = 0;
@@ -311,11 +330,13 @@ __global__ void __launch_bounds__(gemvtc::kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
-bool make_tma_3d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t L, uint64_t row_stride,
-                    uint64_t lstride, uint32_t box_inner, uint32_t box_rows);
+bool make_tma_u8(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                 const uint32_t* box);
+
+static int sub_of(int K) { return K % (2 * gemvtc::kBK) == 0 ? 2 : 1; }
 
 static void plan(int M, int K, int L, int num_sms, int* units, int* grid, int* slots, int* blocks) {
-  const int KT = K / gemvtc::kBK;
+  const int KT = K / (gemvtc::kBK * sub_of(K));
   *blocks = (M / gemvtc::kBM) * L;
   *units = *blocks * KT;
   *grid = *units < num_sms ? *units : num_sms;
@@ -337,20 +358,30 @@ size_t gemv_tc_workspace_bytes(int M, int K, int L, int num_sms) {
          static_cast<size_t>(blocks) * slots * gemvtc::kBM * sizeof(float);
 }
 
-cudaError_t launch_gemv_tc(const GemvTcArgs& g, int num_sms, cudaStream_t stream, const char** why) {
+template <int SUB>
+static cudaError_t launch_sub(const GemvTcArgs& g, int num_sms, cudaStream_t stream, const char** why) {
   using namespace gemvtc;
+  using C = Cfg<SUB>;
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel<SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }
-  const int K2 = g.K / 2;
+  const uint64_t K2 = g.K / 2;
+  // (128-byte column, row, 128-byte column index, batch) views of A and b;
+  // b has one row, the MMA tile's other 31 rows read as zero.
+  const uint64_t da[4] = {128, static_cast<uint64_t>(g.M), K2 / 128, static_cast<uint64_t>(g.L)};
+  const uint64_t sa[3] = {K2, 128, static_cast<uint64_t>(g.a_lstride)};
+  const uint32_t ba[4] = {128, kBM, SUB, 1};
+  const uint64_t db[4] = {128, 1, K2 / 128, static_cast<uint64_t>(g.L)};
+  const uint64_t sb[3] = {K2, 128, static_cast<uint64_t>(g.b_lstride)};
+  const uint32_t bb[4] = {128, kBN, SUB, 1};
   CUtensorMap ta, tb;
-  if (!make_tma_3d_u8(&ta, g.a, K2, g.M, g.L, K2, g.a_lstride, kBKBytes, kBM) ||
-      !make_tma_3d_u8(&tb, g.b, K2, 1, g.L, K2, g.b_lstride, kBKBytes, kBN)) {
+  if (!make_tma_u8(&ta, g.a, 4, da, sa, ba) || !make_tma_u8(&tb, g.b, 4, db, sb, bb)) {
     *why = "cuTensorMapEncodeTiled failed";
     return cudaErrorInvalidValue;
   }
@@ -371,15 +402,20 @@ cudaError_t launch_gemv_tc(const GemvTcArgs& g, int num_sms, cudaStream_t stream
   p.sfa_lstride = g.sfa_lstride;
   p.sfb_lstride = g.sfb_lstride;
   p.c_lstride = g.c_lstride;
-  p.kt_per_block = g.K / kBK;
+  p.kt_per_block = g.K / (kBK * SUB);
   p.blocks_per_l = g.M / kBM;
   p.units = units;
   p.slots = slots;
   p.counters = static_cast<int*>(g.workspace);
   p.ws = reinterpret_cast<float*>(p.counters + kGemvTcMaxCounterBlocks);
   p.status = g.status;
-  gemv_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, p);
+  gemv_tc_kernel<SUB><<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, p);
   return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_tc(const GemvTcArgs& g, int num_sms, cudaStream_t stream, const char** why) {
+  if (sub_of(g.K) == 2) return launch_sub<2>(g, num_sms, stream, why);
+  return launch_sub<1>(g, num_sms, stream, why);
 }
 
 }  // namespace nvfp4
