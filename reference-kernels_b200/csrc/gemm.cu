@@ -220,6 +220,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t sf_col0 = Cfg::kAccBufs * Cfg::kAccCols;
+  if (threadIdx.x == 0) pdl_allow_dependents();
+  pdl_wait();
   bool split_ready = false;  // epilogue threads: this CTA's split partial is in TMEM
 
   if (warp == 0) {
@@ -685,25 +687,11 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
   p.status = g.status;
   p.splits = g.splits > 1 ? g.splits : 1;
   p.num_items = p.num_tiles * p.splits;
-  if (p.splits == 1) {
-    const int grid = p.num_items < num_sms ? p.num_items : num_sms;
-    gemm_kernel<BN, kDual><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tb2, p);
-    return cudaGetLastError();
-  }
-  // Split K: one CTA per (tile, split), the splits of a tile in one cluster.
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.num_items, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = p.splits;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, kDual>, ta, tb, tb2, p);
+  // Without split: a persistent grid.  With split K: one CTA per (tile,
+  // split), the splits of a tile in one cluster.
+  const int grid = p.splits == 1 ? (p.num_items < num_sms ? p.num_items : num_sms) : p.num_items;
+  return launch_pdl(gemm_kernel<BN, kDual>, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, stream, p.splits, ta, tb,
+                    tb2, p);
 }
 
 static int env_int(const char* name) {

@@ -96,6 +96,8 @@ __device__ __forceinline__ void load_item(GemvItem& it, const uint8_t* a_l, cons
 
 __global__ void __launch_bounds__(kGemvMaxWarps * 32) gemv_kernel(const GemvParams p) {
   __shared__ float red[2][kGemvMaxWarps][kGemvRowsPerBatch];
+  if (threadIdx.x == 0) pdl_allow_dependents();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
   const int l = blockIdx.y;
@@ -243,8 +245,7 @@ cudaError_t launch_gemv(const GemvParams& in, int num_sms, cudaStream_t stream) 
   if (per_l > quads) per_l = quads;
   p.ctas_per_l = per_l;
   dim3 grid(per_l, p.L), block(nwarps * 32);
-  gemv_kernel<<<grid, block, 0, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(gemv_kernel, grid, block, 0, stream, 1, p);
 }
 
 }  // namespace nvfp4

@@ -153,6 +153,8 @@ __global__ void __launch_bounds__(gemvtc::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t sf_col0 = kAccBufs * kAccCols;
+  if (threadIdx.x == 0) pdl_allow_dependents();
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -409,8 +411,7 @@ static cudaError_t launch_sub(const GemvTcArgs& g, int num_sms, cudaStream_t str
   p.counters = static_cast<int*>(g.workspace);
   p.ws = reinterpret_cast<float*>(p.counters + kGemvTcMaxCounterBlocks);
   p.status = g.status;
-  gemv_tc_kernel<SUB><<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, p);
-  return cudaGetLastError();
+  return launch_pdl(gemv_tc_kernel<SUB>, dim3(grid), dim3(kThreads), C::kSmemBytes, stream, 1, ta, tb, p);
 }
 
 cudaError_t launch_gemv_tc(const GemvTcArgs& g, int num_sms, cudaStream_t stream, const char** why) {

@@ -5,7 +5,45 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
+#include <cstdlib>
+
 namespace nvfp4 {
+
+// Launch with programmatic stream serialisation (the kernel calls pdl_wait()
+// before touching global memory); optional cluster size.  NVFP4_PDL=0
+// disables the attribute.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       int cluster_x, Args&&... args) {
+  static const bool pdl = [] {
+    const char* e = getenv("NVFP4_PDL");
+    return !(e && e[0] == '0');
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 struct GemvParams {
   const uint8_t* a;    // [L][M][K/2] packed e2m1
