@@ -253,6 +253,52 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+# The reference's task.yml `benchmarks:` shapes and their published
+# speed-of-light times (problems/nvidia/nvfp4_*/task.yml descriptions).
+SUITE = [
+    ("gemv", 7168, 1, 16384, 1, 8.622), ("gemv", 4096, 1, 7168, 8, 17.275), ("gemv", 7168, 1, 2048, 4, 4.317),
+    ("gemm", 128, 7168, 16384, 1, 8.994), ("gemm", 128, 4096, 7168, 1, 2.354), ("gemm", 128, 7168, 2048, 1, 1.333),
+    ("dual", 256, 4096, 7168, 1, 4.708), ("dual", 512, 4096, 7168, 1, 8.714), ("dual", 256, 3072, 4096, 1, 2.125),
+    ("dual", 512, 3072, 7168, 1, 6.535),
+]
+
+
+def run_suite(repeats=20):
+    """Times the reference's benchmark shapes the way its harnesses do:
+    GEMM / dual GEMM: 50 distinct seeded inputs per event pair after an L2
+    flush, time / 50 (eval_better_bench.py:252-268); GEMV: one call per event
+    pair after an L2 flush (eval.py:238-245).  Inputs: the reference's own
+    distributions (generate_input restated in nvfp4_b200.inputs)."""
+    from nvfp4_b200 import inputs
+    flush = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    logs = []
+    for prob, m, n, k, l, sol in SUITE:
+        fn = kernel_fn(prob)
+        count = 1 if prob == "gemv" else 50
+        datas = [inputs.reference_input(prob, m, k, l, 1111 + 42 * (i + 1), n=None if prob == "gemv" else n)
+                 for i in range(count)]
+        for d in datas:
+            fn(d)
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(repeats if prob != "gemv" else 5 * repeats):
+            flush.fill_(1)
+            e0.record()
+            for d in datas:
+                fn(d)
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e3 / count)
+        mean = sum(times) / len(times)
+        line = {"suite": "reference_benchmarks", "problem": prob, "m": m, "n": n, "k": k, "l": l,
+                "us_mean": mean, "us_best": min(times), "sol_us": sol, "sol_over_time": sol / mean}
+        logs.append(mean / sol)
+        print(json.dumps(line), flush=True)
+    geo = math.exp(sum(math.log(x) for x in logs) / len(logs))
+    print(json.dumps({"suite": "reference_benchmarks", "geomean_time_over_sol": geo}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -261,10 +307,14 @@ def main():
     ap.add_argument("--config", default="gemv", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--suite", action="store_true",
+                    help="time the reference's task.yml benchmark shapes (one JSON line each) and exit")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     for d in "mnkl":
         ap.add_argument(f"--{d}", type=int, default=None, help=f"override {d.upper()} (small profiling cases)")
     args = ap.parse_args()
+    if args.suite:
+        return run_suite()
     cfg = CONFIGS[args.config]
     if any(getattr(args, d) is not None for d in "mnkl"):
         cfg = dict(cfg, **{d: getattr(args, d) for d in "mnkl" if getattr(args, d) is not None})

@@ -703,6 +703,41 @@ static int env_int(const char* name) {
 // (the dual GEMM's M=256 shapes, M=128 GEMMs) split K so more SMs work; the
 // splits of a tile form one thread-block cluster and are reduced on chip.
 // NVFP4_GEMM_BN / NVFP4_SPLITS override the choice (tuning only).
+// Clusters of `S` CTAs of this kernel that can be resident at once (clusters
+// must fit inside one GPC, so with ~220 KB of shared memory per CTA this is
+// less than num_sms / S for S = 3, 5, 6, 7, 8).  Cached per device.
+template <int BN, bool kDual>
+static int max_active_clusters(int S) {
+  using Cfg = GemmConfig<BN, kDual>;
+  static int cache[16][9] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 16 || S < 1 || S > 8) return 0;
+  if (!cache[dev][S]) {
+    if (cudaFuncSetAttribute(gemm_kernel<BN, kDual>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
+        cudaSuccess)
+      return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S * 64);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = S;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, kDual>, &cfg) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = -1;  // unknown: fall back to num_sms / S
+    }
+    cache[dev][S] = n;
+  }
+  return cache[dev][S];
+}
+
 GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms) {
   GemmPlan pl;
   const int forced_bn = env_int("NVFP4_GEMM_BN");
@@ -718,6 +753,15 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms) {
   if (splits > ngroups) splits = ngroups;
   if (splits > 8) splits = 8;            // portable cluster size
   if (tiles * splits > num_sms) splits = num_sms / tiles;
+  // All clusters must be resident in one wave: a cluster that starts late
+  // holds up its whole tile.
+  while (splits > 1) {
+    int fit = dual ? max_active_clusters<128, true>(splits)
+                   : (pl.bn == 256 ? max_active_clusters<256, false>(splits) : max_active_clusters<128, false>(splits));
+    if (fit < 0) fit = num_sms / splits;
+    if (tiles <= fit) break;
+    --splits;
+  }
   pl.splits = splits < 1 ? 1 : splits;
   pl.workspace_bytes = 0;
   return pl;
