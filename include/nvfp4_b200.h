@@ -121,6 +121,26 @@ int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* s
                     const void* sfb2_blk, void* c, int M, int N, int K, int L, int64_t a_lstride, int64_t b_lstride,
                     int64_t sfa_lstride, int64_t sfb_lstride, int64_t ldc, int64_t c_lstride, void* stream);
 
+/* NVFP4 quantiser: fp16 (dtype 0) or bf16 (dtype 1) x [L][rows][K] ->
+ * packed e2m1 [L][rows][K/2] + e4m3 scales in the blocked layout, per
+ * 16-element block: s = e4m3_rn_satfinite(amax / (6 * global_scale)),
+ * q = e2m1_rn_satfinite(x / (s * global_scale)) (q = 0 where s == 0), so that
+ * x ~= q * s * global_scale.  Produces the tensors generate_input builds
+ * (nvfp4_gemm/reference.py:56-158, the permuted scale slots via to_blocked,
+ * reference.py:12-24) from real data.  rows % 128 == 0, K % 64 == 0;
+ * x_lstride in elements, packed_lstride / sf_lstride in bytes. */
+int nvfp4_quantize(const void* x, int dtype, void* packed, void* sf_blk, int rows, int K, int L, int64_t x_lstride,
+                   int64_t packed_lstride, int64_t sf_lstride, float global_scale, void* stream);
+
+/* Scale layout conversion between the plain [L][rows][K/16] e4m3 layout
+ * (row stride plain_row_stride bytes) and the 128x4-blocked layout of
+ * to_blocked (nvfp4_gemm/reference.py:12-24); rows % 128 == 0, sk = K/16 with
+ * sk % 4 == 0.  Pure byte permutations. */
+int nvfp4_scales_to_blocked(const void* plain, void* blk, int rows, int sk, int L, int64_t plain_row_stride,
+                            int64_t plain_lstride, int64_t blk_lstride, void* stream);
+int nvfp4_scales_from_blocked(const void* blk, void* plain, int rows, int sk, int L, int64_t plain_row_stride,
+                              int64_t plain_lstride, int64_t blk_lstride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

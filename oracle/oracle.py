@@ -92,6 +92,41 @@ def encode_e4m3(values: np.ndarray) -> np.ndarray:
     return (pos[code].astype(np.uint8) | sign).astype(np.uint8)
 
 
+def encode_e2m1(values: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even, saturating fp32 -> e2m1 code (sign kept, also for zero)."""
+    v = np.asarray(values, dtype=np.float32)
+    mag = np.abs(v)
+    # ties go to the even code: 0.25->0, 0.75->1.0, 1.25->1.0, 1.75->2, 2.5->2, 3.5->4, 5->4
+    code = np.select(
+        [mag <= 0.25, mag < 0.75, mag <= 1.25, mag < 1.75, mag <= 2.5, mag < 3.5, mag <= 5.0],
+        [0, 1, 2, 3, 4, 5, 6], default=7).astype(np.uint8)
+    return code | (np.signbit(v).astype(np.uint8) << 3)
+
+
+def quantize(x: np.ndarray, global_scale: float = 1.0):
+    """NVFP4 quantisation of x [rows, K] (values as float32): per 16-element
+    block s = e4m3_rn_satfinite(amax / (6 g)), q = e2m1_rn_satfinite(x / (s g)),
+    q = 0 where s decodes to 0.  Returns (packed [rows, K/2] uint8 with the even
+    element in the low nibble, plain scale codes [rows, K/16] uint8).  Mirrors
+    the producer step of generate_input (nvfp4_gemm/reference.py:56-158) for
+    real data; divisions are IEEE fp32 round-to-nearest."""
+    x = np.asarray(x, dtype=np.float32)
+    rows, k = x.shape
+    g = np.float32(global_scale)
+    blocks = x.reshape(rows, k // SF_VEC, SF_VEC)
+    amax = np.abs(blocks).max(axis=2)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        s = (amax / (np.float32(6.0) * g)).astype(np.float32)
+    codes = encode_e4m3(np.minimum(s, np.float32(448.0)))
+    d = (E4M3FN_VALUES[codes] * g).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        y = (blocks / d[:, :, None]).astype(np.float32)
+    q = encode_e2m1(y)
+    q = np.where(d[:, :, None] > 0, q, np.uint8(0)).reshape(rows, k)
+    packed = (q[:, 0::2] | (q[:, 1::2] << 4)).astype(np.uint8)
+    return packed, codes.astype(np.uint8)
+
+
 def dequant(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
     """packed [rows, K/2] uint8 and e4m3 codes [rows, K/16] -> float32 [rows, K]."""
     vals = decode_e2m1(packed)

@@ -274,3 +274,50 @@ NVFP4_API int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, con
   return NVFP4_OK;
 }
 
+
+NVFP4_API int nvfp4_quantize(const void* x, int dtype, void* packed, void* sf_blk, int rows, int K, int L,
+                             int64_t x_lstride, int64_t packed_lstride, int64_t sf_lstride, float global_scale,
+                             void* stream) {
+  if (!x || !packed || !sf_blk) return fail(NVFP4_ERR_NULL, "nvfp4_quantize: null pointer");
+  if (dtype != 0 && dtype != 1) return fail(NVFP4_ERR_SHAPE, "nvfp4_quantize: dtype must be 0 (fp16) or 1 (bf16)");
+  if (rows <= 0 || K <= 0 || L <= 0 || rows % 128 || K % 64)
+    return fail(NVFP4_ERR_SHAPE, "nvfp4_quantize: rows=%d must be a multiple of 128 and K=%d of 64", rows, K);
+  if (!(global_scale > 0.f)) return fail(NVFP4_ERR_SHAPE, "nvfp4_quantize: global_scale must be > 0");
+  if (!aligned(x, 32) || !aligned(packed, 8) || !aligned(sf_blk, 4) || (x_lstride % 16) || (packed_lstride % 8) ||
+      (sf_lstride % 4))
+    return fail(NVFP4_ERR_ALIGN, "nvfp4_quantize: x needs 32-byte, packed 8-byte, scales 4-byte alignment");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4_ERR_DEVICE, "nvfp4_quantize: no CUDA device");
+  QuantArgs a{x, dtype, packed, sf_blk, rows, K, L, x_lstride, packed_lstride, sf_lstride, global_scale};
+  cudaError_t e = launch_quantize(a, num_sms_of(dev), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "nvfp4_quantize: %s", cudaGetErrorString(e));
+  return NVFP4_OK;
+}
+
+static int scale_layout(const char* name, bool to_blocked, const void* src, void* dst, int rows, int sk, int L,
+                        int64_t plain_row_stride, int64_t plain_lstride, int64_t blk_lstride, void* stream) {
+  if (!src || !dst) return fail(NVFP4_ERR_NULL, "%s: null pointer", name);
+  if (rows <= 0 || sk <= 0 || L <= 0 || rows % 128 || sk % 4)
+    return fail(NVFP4_ERR_SHAPE, "%s: rows=%d must be a multiple of 128 and K/16=%d of 4", name, rows, sk);
+  if (!aligned(src, 4) || !aligned(dst, 4) || (plain_row_stride % 4) || (plain_lstride % 4) || (blk_lstride % 4))
+    return fail(NVFP4_ERR_ALIGN, "%s: bases and strides must be multiples of 4 bytes", name);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4_ERR_DEVICE, "%s: no CUDA device", name);
+  ScaleLayoutArgs a{src, dst, rows, sk, L, plain_row_stride, plain_lstride, blk_lstride};
+  cudaError_t e = launch_scale_layout(a, to_blocked, num_sms_of(dev), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+  return NVFP4_OK;
+}
+
+NVFP4_API int nvfp4_scales_to_blocked(const void* plain, void* blk, int rows, int sk, int L, int64_t plain_row_stride,
+                                      int64_t plain_lstride, int64_t blk_lstride, void* stream) {
+  return scale_layout("nvfp4_scales_to_blocked", true, plain, blk, rows, sk, L, plain_row_stride, plain_lstride,
+                      blk_lstride, stream);
+}
+
+NVFP4_API int nvfp4_scales_from_blocked(const void* blk, void* plain, int rows, int sk, int L,
+                                        int64_t plain_row_stride, int64_t plain_lstride, int64_t blk_lstride,
+                                        void* stream) {
+  return scale_layout("nvfp4_scales_from_blocked", false, blk, plain, rows, sk, L, plain_row_stride, plain_lstride,
+                      blk_lstride, stream);
+}

@@ -93,4 +93,26 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms);
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why);
 cudaError_t launch_dual_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why);
 
+// Quantiser and scale-layout converter (quant.cu).
+struct QuantArgs {
+  const void* x;  // fp16 (dtype 0) or bf16 (dtype 1), [L][rows][K]
+  int dtype;
+  void* packed;  // [L][rows][K/2]
+  void* sf_blk;  // blocked scales
+  int rows, K, L;
+  int64_t x_lstride;       // elements
+  int64_t packed_lstride;  // bytes
+  int64_t sf_lstride;      // bytes
+  float global_scale;
+};
+cudaError_t launch_quantize(const QuantArgs& a, int num_sms, cudaStream_t stream);
+
+struct ScaleLayoutArgs {
+  const void* src;
+  void* dst;
+  int rows, sk, L;
+  int64_t plain_row_stride, plain_lstride, blk_lstride;  // bytes
+};
+cudaError_t launch_scale_layout(const ScaleLayoutArgs& a, bool to_blocked, int num_sms, cudaStream_t stream);
+
 }  // namespace nvfp4

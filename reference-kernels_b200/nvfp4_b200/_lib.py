@@ -20,6 +20,9 @@ EXPORTS = (
     "nvfp4_gemm",
     "nvfp4_dual_gemm",
     "nvfp4_gemv_noalloc",
+    "nvfp4_quantize",
+    "nvfp4_scales_to_blocked",
+    "nvfp4_scales_from_blocked",
 )
 
 _P = ctypes.c_void_p
@@ -51,6 +54,11 @@ def load() -> ctypes.CDLL:
     lib.nvfp4_gemv.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _L, _P]
     lib.nvfp4_gemv_noalloc.restype = _I
     lib.nvfp4_gemv_noalloc.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _L, _L, _P]
+    lib.nvfp4_quantize.restype = _I
+    lib.nvfp4_quantize.argtypes = [_P, _I, _P, _P, _I, _I, _I, _L, _L, _L, ctypes.c_float, _P]
+    for name in ("nvfp4_scales_to_blocked", "nvfp4_scales_from_blocked"):
+        getattr(lib, name).restype = _I
+        getattr(lib, name).argtypes = [_P, _P, _I, _I, _I, _L, _L, _L, _P]
     lib.nvfp4_gemm.restype = _I
     lib.nvfp4_gemm.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _P]
     lib.nvfp4_dual_gemm.restype = _I
