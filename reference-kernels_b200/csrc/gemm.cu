@@ -536,6 +536,296 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ 2-CTA GEMM
+// Pairs of CTAs (a cluster of 2) compute 256x256 tiles with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=64): each CTA loads its own 128
+// rows of A and its own 128 rows of B (half of the tile's N), so per output
+// element each SM streams half the B bytes of the single-CTA 128x256 tile.
+// Scale factors: each CTA holds SFA for its 128 rows and SFB for all 256
+// columns; the leader's scale copiers issue tcgen05.cp.cta_group::2 (each CTA's
+// shared memory into its own TMEM) and its MMA thread issues the pair MMAs.
+// All loads signal the leader's full barrier (.cta_group::2 TMA); MMA
+// completion is multicast to both CTAs' empty / accumulator barriers.  No load
+// uses cluster multicast.
+namespace pair {
+constexpr int kStages = 5;
+constexpr int kA = kBM * kBKBytes;       // 16 KB: this CTA's 128 rows of A
+constexpr int kB = 128 * kBKBytes;       // 16 KB: this CTA's 128 rows of B
+constexpr int kSfa = kSfStageBytes;      // 2 KB
+constexpr int kSfb = 2 * kSfStageBytes;  // 4 KB: both 128-row blocks of the tile's N
+constexpr int kStage = kA + kB + kSfa + kSfb;
+constexpr int kTx = 2 * kStage;  // the leader's full barrier counts both CTAs' bytes
+constexpr int kAccCols = 256;
+constexpr int kSfCols = 48;
+constexpr int kTmemCols = 512;
+static_assert(kAccCols + kStages * kSfCols <= kTmemCols, "TMEM budget");
+static_assert(kStage % 1024 == 0, "stage alignment");
+constexpr int kSmem = 1024 + kStages * kStage + 256;
+}  // namespace pair
+
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t mbar_cluster, int x,
+                                                 int y, int z, uint64_t hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(mbar_cluster), "l"(hint)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d_pair(void* dst, const CUtensorMap* map, uint32_t mbar_cluster, int c2,
+                                                 int c3, int c4, uint64_t hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(0), "r"(0), "r"(c2), "r"(c3), "r"(c4), "r"(mbar_cluster), "l"(hint)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_nvf4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_cp_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Arrive on the barrier at this offset in the CTAs of `mask` when this
+// thread's prior cta_group::2 tcgen05 operations complete.
+__device__ __forceinline__ void tc_commit_pair_mc(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                     const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
+                     const GemmParams p) {
+  using namespace pair;
+  constexpr int S = kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kStage);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* sf_ready = bars + 2 * S;
+  uint64_t* acc_full = bars + 3 * S;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* drain = acc_empty + 1;  // [0] MMA thread, [1..kCopiers] copiers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1 + kCopiers);
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = p.K / kBK;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair_id = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&sf_ready[s], kCopiers);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 2 * 128);
+    for (int d = 0; d <= kCopiers; ++d) mbar_init(drain + d, 1);
+    fence_barrier_init();
+    prefetch_tensormap(&tm_a);
+    prefetch_tensormap(&tm_b);
+    prefetch_tensormap(&tm_sfa);
+    prefetch_tensormap(&tm_sfb);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, kTmemCols);
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t sf_col0 = kAccCols;
+  if (threadIdx.x == 0) pdl_allow_dependents();
+  pdl_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_first();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = pair_id; t < p.num_tiles && !abort_flag; t += npairs) {
+        int mb, nb, l;
+        tile_coords(p, t, mb, nb, l);
+        const int arow = mb * 256 + static_cast<int>(rank) * 128;
+        const int brow = nb * 256 + static_cast<int>(rank) * 128;
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            set_status(p.status, kStatusTimeoutEmpty);
+            abort_flag = 1;
+            break;
+          }
+          uint8_t* st = smem + stage * kStage;
+          const uint32_t bar0 = map_peer(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], kTx);
+          tma_load_3d_pair(st, &tm_a, bar0, kt * kBKBytes, arow, l, pol_a);
+          tma_load_3d_pair(st + kA, &tm_b, bar0, kt * kBKBytes, brow, l, pol_b);
+          tma_load_5d_pair(st + kA + kB, &tm_sfa, bar0, kt, arow / 128, l, pol_a);
+          tma_load_5d_pair(st + kA + kB + kSfa, &tm_sfb, bar0, kt, nb * 2, l, pol_b);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_nvf4(256, 256);
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = pair_id; t < p.num_tiles && !abort_flag && ok; t += npairs) {
+        if (!mbar_wait(acc_empty, acc_phase ^ 1)) {
+          set_status(p.status, kStatusTimeoutAccEmpty);
+          abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&full[stage], phase) || !mbar_wait(&sf_ready[stage], phase)) {
+            set_status(p.status, kStatusTimeoutFull);
+            abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + stage * kStage);
+          const uint32_t sfc = tmem_base + sf_col0 + stage * kSfCols;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kMmaK; ++kk)
+            mma_nvf4_pair(tmem_base, desc_kmajor_sw128(st + kk * (kMmaK / 2)),
+                          desc_kmajor_sw128(st + kA + kk * (kMmaK / 2)), idesc, sfc + 4 * kk, sfc + 16 + 8 * kk,
+                          (kt | kk) != 0 ? 1u : 0u);
+          tc_commit_pair_mc(&empty[stage], 0x3);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair_mc(acc_full, 0x3);
+        acc_phase ^= 1;
+      }
+      tc_commit_pair(drain);
+      mbar_wait(drain, 0);
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------ scale copiers (leader)
+    if (lane == 0 && leader) {
+      const int ci = warp - 6;
+      int stage = 0;
+      uint32_t phase = 0;
+      int total = 0;
+      for (int t = pair_id; t < p.num_tiles; t += npairs) total += KT;
+      for (int i = 0; i < total && !abort_flag; ++i) {
+        if (!mbar_wait(&full[stage], phase)) {
+          set_status(p.status, kStatusTimeoutFull);
+          abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sf = smem_u32(smem + stage * kStage + kA + kB);
+        const uint32_t sfc = tmem_base + sf_col0 + stage * kSfCols;
+        // SFA step kk at column 4*kk; SFB block j of step kk at 16 + 4*(2*kk + j).
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          if (kk % kCopiers == ci) tmem_cp_pair(sfc + 4 * kk, desc_sf_block(sf + kk * kSfBlockBytes));
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            if ((4 + j * 4 + kk) % kCopiers == ci)
+              tmem_cp_pair(sfc + 16 + 4 * (2 * kk + j), desc_sf_block(sf + kSfa + j * kSfStageBytes + kk * kSfBlockBytes));
+        tc_commit_pair(&sf_ready[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      tc_commit_pair(drain + 1 + ci);
+      mbar_wait(drain + 1 + ci, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const uint32_t acc_empty0 = map_peer(smem_u32(acc_empty), 0);
+    uint32_t acc_phase = 0;
+    for (int t = pair_id; t < p.num_tiles; t += npairs) {
+      int mb, nb, l;
+      tile_coords(p, t, mb, nb, l);
+      if (!__all_sync(0xffffffffu, mbar_wait(acc_full, acc_phase))) {
+        if (lane == 0) set_status(p.status, kStatusTimeoutAccFull);
+        abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = mb * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+      __half* crow = p.c + l * p.c_lstride + static_cast<int64_t>(row) * p.ldc + static_cast<int64_t>(nb) * 256;
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < 256; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tacc + c0, r);
+        tmem_wait_ld();
+        store_half_row32(crow + c0, r);
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(acc_empty0);
+      acc_phase ^= 1;
+    }
+  }
+
+  // The leader's MMAs read both CTAs' shared memory and write both TMEMs:
+  // neither CTA frees TMEM or exits before the pair's work has drained.
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -562,13 +852,13 @@ namespace {
 struct TmaKey {
   const void* base;
   int rank;
-  uint64_t dims[4], strides[3];
-  uint32_t box[4];
+  uint64_t dims[5], strides[4];
+  uint32_t box[5];
   bool operator==(const TmaKey& o) const {
     if (base != o.base || rank != o.rank) return false;
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 5; ++i)
       if (dims[i] != o.dims[i] || box[i] != o.box[i]) return false;
-    for (int i = 0; i < 3; ++i)
+    for (int i = 0; i < 4; ++i)
       if (strides[i] != o.strides[i]) return false;
     return true;
   }
@@ -584,13 +874,13 @@ std::mutex g_tma_mutex;
 
 size_t tma_hash(const TmaKey& k) {
   uint64_t h = reinterpret_cast<uint64_t>(k.base) * 0x9E3779B97F4A7C15ull + k.rank;
-  for (int i = 0; i < 4; ++i) h = (h ^ k.dims[i] ^ (uint64_t(k.box[i]) << 40)) * 0xBF58476D1CE4E5B9ull;
-  for (int i = 0; i < 3; ++i) h = (h ^ k.strides[i]) * 0x94D049BB133111EBull;
+  for (int i = 0; i < 5; ++i) h = (h ^ k.dims[i] ^ (uint64_t(k.box[i]) << 40)) * 0xBF58476D1CE4E5B9ull;
+  for (int i = 0; i < 4; ++i) h = (h ^ k.strides[i]) * 0x94D049BB133111EBull;
   return static_cast<size_t>(h >> 40) % kTmaCacheSize;
 }
 }  // namespace
 
-// Byte tensor of rank 3 or 4 (dims[0] innermost, strides in bytes for dims
+// Byte tensor of rank 3..5 (dims[0] innermost, strides in bytes for dims
 // 1..rank-1) with a box of `box` and 128-byte swizzle; out-of-range rows read
 // as zero.  Encoded maps are cached (direct-mapped on the full argument set):
 // encoding costs microseconds of host time, and callers reuse buffers.
@@ -614,15 +904,18 @@ bool make_tma_u8(CUtensorMap* map, const void* base, int rank, const uint64_t* d
   }
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
-  cuuint64_t d[4], st[3];
-  cuuint32_t bx[4], es[4] = {1, 1, 1, 1};
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5] = {1, 1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) {
     d[i] = dims[i];
     bx[i] = box[i];
     if (i > 0) st[i - 1] = strides[i - 1];
   }
+  // Scale-factor maps (inner box of 256 bytes) are plain copies; operand maps
+  // use the 128-byte swizzle tcgen05 descriptors expect.
+  const CUtensorMapSwizzle swz = box[0] == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), d, st, bx, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   std::lock_guard<std::mutex> lock(g_tma_mutex);
@@ -767,7 +1060,73 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms) {
   return pl;
 }
 
+static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {
+  static bool attr_done[64] = {false};
+  static int max_pairs[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::kSmem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pair::kSmem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel, &cfg) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = num_sms / 2;
+    }
+    max_pairs[dev] = n;
+    attr_done[dev] = true;
+  }
+  const uint64_t K2 = g.K / 2, KT = g.K / kBK;
+  CUtensorMap ta, tb, tsfa, tsfb;
+  const uint64_t dsa[5] = {256, 8, KT, static_cast<uint64_t>(g.M / 128), static_cast<uint64_t>(g.L)};
+  const uint64_t ssa[4] = {256, 2048, static_cast<uint64_t>(g.K) * 8, static_cast<uint64_t>(g.sfa_lstride)};
+  const uint32_t bsa[5] = {256, 8, 1, 1, 1};
+  const uint64_t dsb[5] = {256, 8, KT, static_cast<uint64_t>(g.N / 128), static_cast<uint64_t>(g.L)};
+  const uint64_t ssb[4] = {256, 2048, static_cast<uint64_t>(g.K) * 8, static_cast<uint64_t>(g.sfb_lstride)};
+  const uint32_t bsb[5] = {256, 8, 1, 2, 1};
+  if (!make_operand_map(&ta, g.a, K2, g.M, g.L, g.a_lstride, 128) ||
+      !make_operand_map(&tb, g.b, K2, g.N, g.L, g.b_lstride, 128) || !make_tma_u8(&tsfa, g.sfa, 5, dsa, ssa, bsa) ||
+      !make_tma_u8(&tsfb, g.sfb, 5, dsb, ssb, bsb)) {
+    *why = "cuTensorMapEncodeTiled failed";
+    return cudaErrorInvalidValue;
+  }
+  GemmParams p{};
+  p.c = static_cast<__half*>(g.c);
+  p.M = g.M;
+  p.N = g.N;
+  p.K = g.K;
+  p.L = g.L;
+  p.ldc = g.ldc;
+  p.c_lstride = g.c_lstride;
+  p.tiles_m = g.M / 256;
+  p.tiles_n = g.N / 256;
+  p.num_tiles = p.tiles_m * p.tiles_n * g.L;
+  p.group_m = p.tiles_m < 8 ? p.tiles_m : 8;
+  p.status = g.status;
+  p.splits = 1;
+  p.num_items = p.num_tiles;
+  int pairs = max_pairs[dev < 64 ? dev : 0];
+  if (pairs > p.num_tiles) pairs = p.num_tiles;
+  if (pairs < 1) pairs = 1;
+  return launch_pdl(gemm_pair_kernel, dim3(2 * pairs), dim3(kThreads), pair::kSmem, stream, 2, ta, tb, tsfa, tsfb,
+                    p);
+}
+
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {
+  const char* pe = getenv("NVFP4_PAIR");  // "0": keep 1-CTA tiles (comparison / tests)
+  const bool pair_ok = !(pe && pe[0] == '0');
+  if (g.bn == 256 && g.splits == 1 && g.M % 256 == 0 && pair_ok) return launch_pair(g, num_sms, stream, why);
   if (g.bn == 256) return launch_impl<256, false>(g, num_sms, stream, why);
   return launch_impl<128, false>(g, num_sms, stream, why);
 }

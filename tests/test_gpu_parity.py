@@ -141,3 +141,21 @@ def test_dual_benchmark_shapes(m, n, k):
     ref = scaled_mm_ref("dual", data)
     out = run("dual", data)
     assert_match(out, ref, f"dual {m}x{n}x{k} vs _scaled_mm")
+
+
+@pytest.mark.parametrize("m,n,k,l", [(256, 256, 256, 1), (512, 1024, 2048, 1), (768, 512, 1024, 2), (2304, 4608, 7168, 1)])
+def test_pair_gemm_matches_single_cta_and_oracle(m, n, k, l, monkeypatch):
+    """2-CTA (cta_group::2, 256x256 tiles) GEMM against the 1-CTA kernel
+    (bit-identical: same fp32 accumulation order per K step is not guaranteed,
+    so the tolerance check is the gate) and the CPU oracle on small shapes."""
+    monkeypatch.setenv("NVFP4_SPLITS", "1")
+    data = inputs.baseline_input("gemm", m, k, l, 21, n=n)
+    monkeypatch.setenv("NVFP4_PAIR", "0")
+    single = run("gemm", data).clone()
+    monkeypatch.setenv("NVFP4_PAIR", "1")
+    pair1 = run("gemm", data).clone()
+    pair2 = run("gemm", data).clone()
+    assert torch.equal(pair1, pair2)
+    assert_match(pair1, single, f"pair vs single {m}x{n}x{k}x{l}")
+    if m * n * k <= 768 * 1024 * 2048:
+        assert_match(pair1, oracle_ref("gemm", data), f"pair vs oracle {m}x{n}x{k}x{l}")
