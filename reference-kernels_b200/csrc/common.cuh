@@ -23,8 +23,8 @@ enum DeviceStatus : int {
   kStatusTimeoutAccEmpty = 4, // MMA warp waited too long for the epilogue
 };
 
-// Default wait budget: 2 s of wall time per wait.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Wait budget: 1 s of wall time per wait (normal waits last microseconds).
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -73,6 +73,7 @@ struct GemmParams {
   int64_t ldc, c_lstride;                          // elements
   int tiles_m, tiles_n, num_tiles;
   int group_m;  // raster: groups of group_m M-blocks sweep all N-blocks
+  int inject;   // test hook: 1 = CTA 0 withholds its first A load (its pipeline waits then run out)
   int splits;   // K splits per tile (1 = none); work item = tile * splits + split.
                 // With splits > 1 the kernel is launched with clusters of
                 // `splits` CTAs, one item per CTA, cluster = tile.
@@ -250,7 +251,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* st = tiles + stage * Cfg::kStageBytes;
           uint8_t* sf = sfbuf + stage * Cfg::kSfOps * kSfStageBytes;
           mbar_arrive_expect_tx(&full[stage], Cfg::kTxBytes);
-          tma_load_3d(st, &tm_a, &full[stage], kt * kBKBytes, mb * kBM, l, pol_a);
+          if (!(p.inject && blockIdx.x == 0 && it == 0 && kt == k0))
+            tma_load_3d(st, &tm_a, &full[stage], kt * kBKBytes, mb * kBM, l, pol_a);
           tma_load_3d(st + Cfg::kABytes, &tm_b, &full[stage], kt * kBKBytes, nb * BN, l, pol_b);
           if (kDual) tma_load_3d(st + Cfg::kABytes + Cfg::kBBytes, &tm_b2, &full[stage], kt * kBKBytes, nb * BN, l, pol_b);
           bulk_load(sf, sfa_src + kt * kSfStageBytes, kSfStageBytes, &full[stage], pol_a);
@@ -980,6 +982,10 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
   p.status = g.status;
   p.splits = g.splits > 1 ? g.splits : 1;
   p.num_items = p.num_tiles * p.splits;
+  // Test hook for the bounded-wait path (tests/test_failure_detection.py):
+  // the kernel then reports a pipeline timeout instead of hanging.
+  const char* fi = getenv("NVFP4_FAULT_INJECT");
+  p.inject = (fi && fi[0] == '1' && p.splits == 1) ? 1 : 0;
   // Without split: a persistent grid.  With split K: one CTA per (tile,
   // split), the splits of a tile in one cluster.
   const int grid = p.splits == 1 ? (p.num_items < num_sms ? p.num_items : num_sms) : p.num_items;
