@@ -59,25 +59,26 @@ static int num_sms_of(int dev) {
   return cache[dev];
 }
 
-// Per-device workspace for kernels that combine partial results across CTAs
-// (the tensor-core GEMV).  Allocated on the first call that needs it (and
+// Per-device workspaces for kernels that combine partial results across CTAs
+// (kind 0: the tensor-core GEMV; kind 1: the stream-K GEMM).  Allocated on the first call that needs it (and
 // grown when a later call needs more), zeroed once; the kernels leave it
 // zeroed.  Calls on one device share it, so they must not overlap on the GPU.
 struct DeviceWorkspace {
   void* ptr = nullptr;
   size_t bytes = 0;
 };
-static DeviceWorkspace g_ws[64];
+enum { kWsGemv = 0, kWsGemm = 1 };
+static DeviceWorkspace g_ws[2][64];
 static std::mutex g_ws_mutex;
 
-static void* workspace_for(int dev, size_t bytes, cudaStream_t stream, cudaError_t* err) {
+static void* workspace_for(int kind, int dev, size_t bytes, cudaStream_t stream, cudaError_t* err) {
   *err = cudaSuccess;
   if (dev < 0 || dev >= 64) {
     *err = cudaErrorInvalidDevice;
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(g_ws_mutex);
-  DeviceWorkspace& w = g_ws[dev];
+  DeviceWorkspace& w = g_ws[kind][dev];
   if (w.bytes >= bytes) return w.ptr;
   if (w.ptr) {
     // earlier launches may still read the old buffer
@@ -146,7 +147,7 @@ NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa_blk, cons
     g.c_lstride = c_lstride;
     g.workspace_bytes = gemv_tc_workspace_bytes(M, K, L, num_sms_of(dev));
     cudaError_t e = cudaSuccess;
-    g.workspace = workspace_for(dev, g.workspace_bytes, s, &e);
+    g.workspace = workspace_for(kWsGemv, dev, g.workspace_bytes, s, &e);
     if (!g.workspace) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: workspace: %s", cudaGetErrorString(e));
     g.status = status_ptr(dev);
     const char* why = nullptr;
@@ -225,6 +226,14 @@ NVFP4_API int nvfp4_gemm(const void* a, const void* b, const void* sfa_blk, cons
   const GemmPlan pl = gemm_plan(M, N, K, L, false, num_sms_of(dev));
   g.bn = pl.bn;
   g.splits = pl.splits;
+  g.streamk = pl.streamk;
+  g.pair = pl.pair;
+  if (pl.workspace_bytes) {
+    cudaError_t we;
+    g.workspace = workspace_for(kWsGemm, dev, pl.workspace_bytes, static_cast<cudaStream_t>(stream), &we);
+    if (!g.workspace) return fail(NVFP4_ERR_CUDA, "nvfp4_gemm: workspace: %s", cudaGetErrorString(we));
+    g.workspace_bytes = pl.workspace_bytes;
+  }
   const char* why = nullptr;
   cudaError_t e = launch_gemm(g, num_sms_of(dev), static_cast<cudaStream_t>(stream), &why);
   if (e != cudaSuccess)

@@ -21,6 +21,7 @@ enum DeviceStatus : int {
   kStatusTimeoutEmpty = 2,    // TMA warp waited too long for a free stage
   kStatusTimeoutAccFull = 3,  // epilogue waited too long for an accumulator
   kStatusTimeoutAccEmpty = 4, // MMA warp waited too long for the epilogue
+  kStatusTimeoutPeer = 5,     // a CTA waited too long for another CTA's partial sums
 };
 
 // Wait budget: 1 s of wall time per wait (normal waits last microseconds).
@@ -91,6 +92,46 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *flag != 0 (acquire). Returns false when the deadline passed.
+__device__ __forceinline__ bool flag_wait(const int* flag) {
+  if (ld_acquire_gpu(flag)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_gpu(flag)) return true;
+    if ((i & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+// As mbar_wait, with cluster-scope acquire: for barriers that threads of
+// another CTA of the cluster arrive on (release.cluster).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((i & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) return false;
   }
 }
@@ -185,6 +226,14 @@ __device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdes
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
+// Each thread of the warp writes its four 32-bit registers to TMEM lane
+// (lane quarter of the warp) * 32 + laneid, columns taddr .. taddr+3.
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, uint4 v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 32 consecutive 32-bit columns: thread t gets row (lane base + t).

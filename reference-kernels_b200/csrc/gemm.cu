@@ -5,22 +5,23 @@
 //   Dual:  C[m,n,l] = fp16( silu(A.B1^T) * (A.B2^T) ), both products in fp32
 //          ref_kernel of problems/nvidia/nvfp4_dual_gemm/reference.py:27-77
 //
-// Structure (one CTA per SM, persistent, 8 warps):
+// Structure (one CTA per SM, persistent, 10 warps):
 //   warp 0      TMA producer: A/B tiles with 128-byte swizzle through
 //               cp.async.bulk.tensor, the 128x4-blocked scale factors through
 //               plain cp.async.bulk (each 128-row block of scales for a
 //               256-wide K tile is one contiguous 2 KB run), into a ring of
 //               kStages shared-memory stages guarded by full/empty mbarriers.
-//   warps 6, 7  scale copiers: per K tile, tcgen05.cp moves the stage's scale
-//               blocks into TMEM (32x128b, replicated to the four lane
-//               quarters), the copies split between the two warps, which then
-//               commit to sf_ready[stage].  Copies issued by the MMA thread
-//               itself serialise with its MMAs (measured ~45 tensor-pipe
-//               cycles per copy); issued from other threads they overlap, and
-//               two copier threads beat one (measured; four are slower).
+//   warps 6..9  scale copiers, one per TMEM lane quarter: per K tile each
+//               reads the stage's scale blocks from shared memory and writes
+//               them into its 32 TMEM lanes with tcgen05.st (the blocks
+//               replicated to the four lane quarters, the layout the MMA
+//               reads), then arrives on sf_ready[stage].  tcgen05.cp of the
+//               same blocks costs ~45 tensor-pipe cycles each and competes
+//               with the MMAs for the pipe (measured); the stores do not.
 //   warp 1      TMEM owner and MMA issuer: per K tile, four tcgen05.mma
-//               kind::mxf4nvf4 (M=128, N=BN, K=64 each; two per step for the
-//               dual GEMM, sharing the A tile) accumulate in fp32 in TMEM;
+//               kind::mxf4nvf4 (M=128, N=BN, K=64 each; for the dual GEMM
+//               N=256 over the adjacent B1 and B2 tiles, so A is read once
+//               for both products) accumulate in fp32 in TMEM;
 //               tcgen05.commit releases the stage and, after the last K tile,
 //               hands the accumulator to the epilogue.
 //   warps 2..5  epilogue: tcgen05.ld rows of the accumulator(s), optional
@@ -36,14 +37,49 @@
 
 namespace nvfp4 {
 
+// Optional per-CTA timing of the pipeline waits (build with -DNVFP4_TRACE;
+// read with nvfp4_dbg_gemm_trace).  Slots per CTA: 0 MMA waiting for a stage,
+// 1 MMA waiting for its scales, 2 MMA role total, 3 producer waiting for a
+// free stage, 4 scale writer waiting for a stage, 5 scale writer total,
+// 6 epilogue waiting for an accumulator, 7 epilogue total (SM cycles).
+#ifdef NVFP4_TRACE
+__device__ unsigned long long g_gemm_trace[1024 * 8];
+#define TRW(slot, expr)                      \
+  ({                                         \
+    const long long _t0 = clock64();         \
+    const bool _r = (expr);                  \
+    trace[slot] += clock64() - _t0;          \
+    _r;                                      \
+  })
+#define TRACE_DECL unsigned long long trace[8] = {0, 0, 0, 0, 0, 0, 0, 0}; const long long trace_t0 = clock64()
+#define TRACE_TOTAL(slot) trace[slot] = clock64() - trace_t0
+#define TRACE_FLUSH()                                                             \
+  do {                                                                            \
+    if (lane == 0)                                                                \
+      for (int _i = 0; _i < 8; ++_i)                                              \
+        if (trace[_i]) g_gemm_trace[blockIdx.x * 8 + _i] = trace[_i];             \
+  } while (0)
+#else
+#define TRW(slot, expr) (expr)
+#define TRACE_DECL
+#define TRACE_TOTAL(slot)
+#define TRACE_FLUSH()
+#endif
+
 constexpr int kBM = 128;
 constexpr int kBK = 256;          // K elements per stage (128 bytes per row)
 constexpr int kBKBytes = kBK / 2;
 constexpr int kMmaK = 64;         // K per tcgen05.mma for kind::mxf4nvf4
+constexpr int kStreamKFlagBytes = 4096;  // stream-K flags at the workspace start (<= 1024 CTAs)
 constexpr int kSfBlockBytes = 512;  // one 128-row x 4-scale block
 constexpr int kSfStageBytes = kSfBlockBytes * (kBK / kMmaK);  // 2 KB per operand per stage
-constexpr int kCopiers = 2;  // scale-copier warps (6, 7)
+// Scale copiers of the 1-CTA kernel: four warps (6..9), one per TMEM lane
+// quarter, write the scales with tcgen05.st.
+constexpr int kCopiers = 4;
 constexpr int kThreads = 192 + 32 * kCopiers;
+// The 2-CTA kernel: four scale-writer warps per CTA as well.
+constexpr int kPairCopiers = 4;
+constexpr int kPairThreads = 192 + 32 * kPairCopiers;
 
 template <int BN, bool kDual>
 struct GemmConfig {
@@ -78,6 +114,16 @@ struct GemmParams {
                 // With splits > 1 the kernel is launched with clusters of
                 // `splits` CTAs, one item per CTA, cluster = tile.
   int num_items;
+  // Stream-K (splits == 1 only): the tiles x K-tiles "units", in tile-major
+  // order, are cut into gridDim.x equal contiguous ranges, one per CTA.  A CTA
+  // whose range starts inside a tile (its first segment) writes that partial
+  // tile, fp32, to slot blockIdx.x of sk_partial and raises sk_flag[blockIdx.x];
+  // the CTA holding the tile's first K tiles (its last segment) adds the
+  // partials of the following CTAs, in CTA order, and writes C.
+  int streamk;
+  int64_t units;
+  float* sk_partial;  // gridDim.x slots of kBM x BN floats
+  int* sk_flag;       // gridDim.x flags, 0 between launches
   int* status;
 };
 
@@ -86,6 +132,39 @@ __device__ __forceinline__ void split_range(int KT, int splits, int s, int& k0, 
   k0 = (s * KT) / splits;
   k1 = ((s + 1) * KT) / splits;
 }
+
+// First unit of CTA b's stream-K range.
+__device__ __forceinline__ int64_t sk_begin(const GemmParams& p, int b) {
+  return (static_cast<int64_t>(b) * p.units) / gridDim.x;
+}
+
+// The work items of this CTA, in order: (tile, K-tile range).  Every warp role
+// walks the same sequence.
+struct WorkIter {
+  int64_t u, u_end;
+  int it;
+  __device__ __forceinline__ explicit WorkIter(const GemmParams& p) {
+    it = blockIdx.x;
+    u = p.streamk ? sk_begin(p, blockIdx.x) : 0;
+    u_end = p.streamk ? sk_begin(p, blockIdx.x + 1) : 0;
+  }
+  __device__ __forceinline__ bool next(const GemmParams& p, int KT, int& t, int& k0, int& k1) {
+    if (p.streamk) {
+      if (u >= u_end) return false;
+      t = static_cast<int>(u / KT);
+      k0 = static_cast<int>(u - static_cast<int64_t>(t) * KT);
+      const int64_t rem = u_end - u;
+      k1 = (KT - k0 > rem) ? k0 + static_cast<int>(rem) : KT;
+      u += k1 - k0;
+      return true;
+    }
+    if (it >= p.num_items) return false;
+    t = it / p.splits;
+    split_range(KT, p.splits, it - t * p.splits, k0, k1);
+    it += gridDim.x;
+    return true;
+  }
+};
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -192,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = bars + 3 * S;
   uint64_t* acc_empty = acc_full + Cfg::kAccBufs;
   uint64_t* drain = acc_empty + Cfg::kAccBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1 + kCopiers);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -209,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 128);
     }
-    for (int d = 0; d <= kCopiers; ++d) mbar_init(drain + d, 1);
+    mbar_init(drain, 1);
     fence_barrier_init();
     prefetch_tensormap(&tm_a);
     prefetch_tensormap(&tm_b);
@@ -223,6 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sf_col0 = Cfg::kAccBufs * Cfg::kAccCols;
   if (threadIdx.x == 0) pdl_allow_dependents();
   pdl_wait();
+  TRACE_DECL;
   bool split_ready = false;  // epilogue threads: this CTA's split partial is in TMEM
 
   if (warp == 0) {
@@ -232,10 +312,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_b = policy_evict_first();
       int stage = 0;
       uint32_t phase = 0;
-      for (int it = blockIdx.x; it < p.num_items && !abort_flag; it += gridDim.x) {
-        const int t = it / p.splits;
-        int k0, k1;
-        split_range(KT, p.splits, it - t * p.splits, k0, k1);
+      WorkIter wi(p);
+      int t, k0, k1, item = 0;
+      for (; !abort_flag && wi.next(p, KT, t, k0, k1); ++item) {
         int mb, nb, l;
         tile_coords(p, t, mb, nb, l);
         const uint8_t* sfa_src = p.sfa + l * p.sfa_lstride + static_cast<int64_t>(mb) * p.K * 8;
@@ -243,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* sfb2_src =
             kDual ? p.sfb2 + l * p.sfb2_lstride + static_cast<int64_t>(nb) * (BN / 128) * p.K * 8 : nullptr;
         for (int kt = k0; kt < k1; ++kt) {
-          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+          if (!TRW(3, mbar_wait(&empty[stage], phase ^ 1))) {
             set_status(p.status, kStatusTimeoutEmpty);
             abort_flag = 1;
             break;
@@ -251,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* st = tiles + stage * Cfg::kStageBytes;
           uint8_t* sf = sfbuf + stage * Cfg::kSfOps * kSfStageBytes;
           mbar_arrive_expect_tx(&full[stage], Cfg::kTxBytes);
-          if (!(p.inject && blockIdx.x == 0 && it == 0 && kt == k0))
+          if (!(p.inject && blockIdx.x == 0 && item == 0 && kt == k0))
             tma_load_3d(st, &tm_a, &full[stage], kt * kBKBytes, mb * kBM, l, pol_a);
           tma_load_3d(st + Cfg::kABytes, &tm_b, &full[stage], kt * kBKBytes, nb * BN, l, pol_b);
           if (kDual) tma_load_3d(st + Cfg::kABytes + Cfg::kBBytes, &tm_b2, &full[stage], kt * kBKBytes, nb * BN, l, pol_b);
@@ -278,13 +357,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_nvf4(kBM, BN);
+      constexpr uint32_t idesc_dual = idesc_nvf4(kBM, 2 * BN);
+      static_assert(!kDual || BN == 128, "dual GEMM: B1|B2 form one N=256 operand");
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int it = blockIdx.x; it < p.num_items && !abort_flag; it += gridDim.x) {
-        int k0, k1;
-        split_range(KT, p.splits, it % p.splits, k0, k1);
+      WorkIter wi(p);
+      int t, k0, k1;
+      while (!abort_flag && wi.next(p, KT, t, k0, k1)) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1)) {
           set_status(p.status, kStatusTimeoutAccEmpty);
           abort_flag = 1;
@@ -294,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d0 = tmem_base + acc * Cfg::kAccCols;
         bool ok = true;
         for (int kt = k0; kt < k1; ++kt) {
-          if (!mbar_wait(&full[stage], phase) || !mbar_wait(&sf_ready[stage], phase)) {
+          if (!TRW(0, mbar_wait(&full[stage], phase)) || !TRW(1, mbar_wait(&sf_ready[stage], phase))) {
             set_status(p.status, kStatusTimeoutFull);
             abort_flag = 1;
             ok = false;
@@ -308,11 +389,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t adesc = desc_kmajor_sw128(st + kk * (kMmaK / 2));
             const uint64_t bdesc = desc_kmajor_sw128(st + Cfg::kABytes + kk * (kMmaK / 2));
             const uint32_t accum = (kt != k0 || kk != 0) ? 1u : 0u;
-            mma_nvf4(d0, adesc, bdesc, idesc, sfc + 4 * kk, sfc + 16 + 4 * kk * (BN / 128), accum);
             if (kDual) {
-              const uint64_t b2desc = desc_kmajor_sw128(st + Cfg::kABytes + Cfg::kBBytes + kk * (kMmaK / 2));
-              mma_nvf4(d0 + BN, adesc, b2desc, idesc, sfc + 4 * kk, sfc + 16 + 16 * (BN / 128) + 4 * kk * (BN / 128),
-                       accum);
+              // The B1 and B2 tiles sit back to back in shared memory: one
+              // N=2*BN MMA (B2 as rows BN.. of B) reads A once for both
+              // products; accumulator columns [0,BN) = A.B1, [BN,2BN) = A.B2.
+              mma_nvf4(d0, adesc, bdesc, idesc_dual, sfc + 4 * kk, sfc + 16 + 8 * kk, accum);
+            } else {
+              mma_nvf4(d0, adesc, bdesc, idesc, sfc + 4 * kk, sfc + 16 + 4 * kk * (BN / 128), accum);
             }
           }
           tc_commit(&empty[stage]);
@@ -334,51 +417,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 6) {
     // ------------------------------------------------------------ scale copiers
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int total = 0;
-      for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
-        int k0, k1;
-        split_range(KT, p.splits, it % p.splits, k0, k1);
-        total += k1 - k0;
+    // Warps 6..9, one per TMEM lane quarter (warp % 4).  Per stage every
+    // warp reads the stage's 512-byte scale blocks from shared memory (lane
+    // i takes the 16 bytes of rows i, i+32, i+64, i+96) and writes them with
+    // tcgen05.st to its 32 lanes, four columns per block: together the four
+    // warps leave TMEM exactly as tcgen05.cp.32x128b.warpx4 would (the
+    // block replicated to all four lane quarters).  Layout per stage: SFA
+    // at columns [0,16) (MMA step kk at 4*kk), then the B scales: 128-row
+    // block j of step kk at 16 + 4*(kk*NB + j), NB = 128-row blocks per MMA
+    // (BN/128, or 2 for the dual GEMM's B1|B2), the order an N=128*NB MMA
+    // reads them in.
+    // tcgen05.st does not enter the tensor pipe, so unlike tcgen05.cp
+    // (~45 pipe cycles per block) it does not take issue slots from the MMAs.
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    int stage = 0;
+    uint32_t phase = 0;
+    int total = 0;
+    {
+      WorkIter wi(p);
+      int t, k0, k1;
+      while (wi.next(p, KT, t, k0, k1)) total += k1 - k0;
+    }
+    for (int i = 0; i < total; ++i) {
+      const bool got = TRW(4, mbar_wait(&full[stage], phase));
+      if (!__all_sync(0xffffffffu, got && !abort_flag)) {
+        if (lane == 0 && !got) set_status(p.status, kStatusTimeoutFull);
+        abort_flag = 1;
+        break;
       }
-      for (int i = 0; i < total && !abort_flag; ++i) {
-        if (!mbar_wait(&full[stage], phase)) {
-          set_status(p.status, kStatusTimeoutFull);
-          abort_flag = 1;
-          break;
+      tc_fence_after();
+      const uint8_t* sf = sfbuf + stage * Cfg::kSfOps * kSfStageBytes + lane * 16;
+      const uint32_t sfc = tmem_base + lane_base + sf_col0 + stage * Cfg::kSfCols;
+#pragma unroll
+      for (int r = 0; r < Cfg::kSfOps; ++r)
+#pragma unroll
+        for (int kk = 0; kk < kBK / kMmaK; ++kk) {
+          const uint4 v = *reinterpret_cast<const uint4*>(sf + r * kSfStageBytes + kk * kSfBlockBytes);
+          // Dual: B1 and B2 are the two 128-row blocks of one N=256 operand.
+          const int col = r == 0  ? 4 * kk
+                          : kDual ? 16 + 4 * (2 * kk + (r - 1))
+                                  : 16 + 4 * (kk * (BN / 128) + (r - 1) % (BN / 128));
+          tmem_st_32x32b_x4(sfc + col, v);
         }
-        tc_fence_after();
-        const uint32_t sf = smem_u32(sfbuf + stage * Cfg::kSfOps * kSfStageBytes);
-        const uint32_t sfc = tmem_base + sf_col0 + stage * Cfg::kSfCols;
-        // Per stage: SFA at columns [0,16) (MMA step kk at 4*kk), then per B
-        // operand 16*(BN/128) columns where the scales of 128-row block j for
-        // step kk sit at 4*(kk*(BN/128) + j), the column order an N=BN MMA
-        // reads them in.
-        // The copies of a stage are dealt round-robin to the copier warps,
-        // which issue them in parallel; sf_ready completes after all commit.
-        const int ci = warp - 6;
-#pragma unroll
-        for (int kk = 0; kk < kBK / kMmaK; ++kk)
-          if (kk % kCopiers == ci) tmem_cp_32x128b_x4(sfc + 4 * kk, desc_sf_block(sf + kk * kSfBlockBytes));
-#pragma unroll
-        for (int op = 0; op < Cfg::kNB; ++op)
-#pragma unroll
-          for (int j = 0; j < BN / 128; ++j)
-#pragma unroll
-            for (int kk = 0; kk < kBK / kMmaK; ++kk)
-              if ((kBK / kMmaK + (op * (BN / 128) + j) * (kBK / kMmaK) + kk) % kCopiers == ci)
-                tmem_cp_32x128b_x4(sfc + 16 + op * 16 * (BN / 128) + 4 * (kk * (BN / 128) + j),
-                                   desc_sf_block(sf + (1 + op * (BN / 128) + j) * kSfStageBytes + kk * kSfBlockBytes));
-        tc_commit(&sf_ready[stage]);
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1;
-        }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sf_ready[stage]);
+      if (++stage == S) {
+        stage = 0;
+        phase ^= 1;
       }
-      tc_commit(drain + 1 + (warp - 6));
-      mbar_wait(drain + 1 + (warp - 6), 0);
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -386,13 +474,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool split = p.splits > 1;
-    for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
-      const int t = it / p.splits;
+    WorkIter wi(p);
+    int t, k0, k1;
+    while (wi.next(p, KT, t, k0, k1)) {
       int mb, nb, l;
       tile_coords(p, t, mb, nb, l);
       // All lanes (and, with split K, all four epilogue warps, which meet at
       // named barriers below) must agree before the collective tcgen05.ld.
-      const bool got = mbar_wait(&acc_full[acc], acc_phase);
+      const bool got = TRW(6, mbar_wait(&acc_full[acc], acc_phase));
       if (split ? !epi_all(got) : !__all_sync(0xffffffffu, got)) {
         if (lane == 0) set_status(p.status, kStatusTimeoutAccFull);
         abort_flag = 1;
@@ -403,7 +492,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = mb * kBM + rloc;
       __half* crow = p.c + l * p.c_lstride + static_cast<int64_t>(row) * p.ldc + static_cast<int64_t>(nb) * BN;
       const uint32_t tacc = tmem_base + acc * Cfg::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      if (!split) {
+      if (!kDual && !split && p.streamk && k0 > 0) {
+        // Stream-K contributor: this CTA holds K tiles [k0, k1) of tile t
+        // (the first segment of its range).  Partial sums go to its slot as
+        // [column group][float4 index][row][4], one coalesced 512-byte row
+        // of float4 per warp instruction; then the flag is raised.
+        float4* dst = reinterpret_cast<float4*>(p.sk_partial) + static_cast<int64_t>(blockIdx.x) * (kBM * BN / 4) + rloc;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tacc + c0, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[((c0 / 32) * 8 + i) * kBM] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                                         __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        epi_bar();
+        if (threadIdx.x == 64) {
+          __threadfence();
+          st_release_gpu(p.sk_flag + blockIdx.x, 1);
+        }
+      } else if (!split) {
+        // Stream-K finaliser (K tiles [0, k1) with k1 < KT, the last segment
+        // of this CTA's range): the rest of the tile was computed by the
+        // following CTAs [blockIdx.x + 1, c_end) as their first segments.
+        int c_end = blockIdx.x + 1;
+        if (p.streamk && k1 < KT) {
+          const int64_t tile_end = static_cast<int64_t>(t + 1) * KT;
+          while (c_end < static_cast<int>(gridDim.x) && sk_begin(p, c_end) < tile_end) ++c_end;
+          bool ok = true;
+          if (threadIdx.x == 64) {
+            for (int c = blockIdx.x + 1; c < c_end && ok; ++c) ok = flag_wait(p.sk_flag + c);
+            if (ok)
+              for (int c = blockIdx.x + 1; c < c_end; ++c) p.sk_flag[c] = 0;  // ready for the next launch
+            else
+              set_status(p.status, kStatusTimeoutPeer);
+          }
+          if (!epi_all(ok)) {
+            abort_flag = 1;
+            break;
+          }
+        }
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
           uint32_t r[32];
@@ -417,6 +549,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               r[i] = __float_as_uint(silu_mul(__uint_as_float(r[i]), __uint_as_float(r2[i])));
           } else {
             tmem_wait_ld();
+            // Own partial first, then the contributors' in CTA order: the
+            // same order on every call with the same grid.
+            for (int c = blockIdx.x + 1; c < c_end; ++c) {
+              const float4* src = reinterpret_cast<const float4*>(p.sk_partial) +
+                                  static_cast<int64_t>(c) * (kBM * BN / 4) + (c0 / 32) * 8 * kBM + rloc;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 v = __ldcg(src + i * kBM);
+                r[4 * i] = __float_as_uint(__uint_as_float(r[4 * i]) + v.x);
+                r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) + v.y);
+                r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) + v.z);
+                r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) + v.w);
+              }
+            }
           }
           store_half_row32(crow + c0, r);
         }
@@ -529,6 +675,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+#ifdef NVFP4_TRACE
+  if (warp == 1) TRACE_TOTAL(2);
+  if (warp == 6) TRACE_TOTAL(5);
+  if (warp == 2) TRACE_TOTAL(7);
+  if (warp <= 2 || warp == 6) TRACE_FLUSH();
+#endif
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -542,13 +694,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Pairs of CTAs (a cluster of 2) compute 256x256 tiles with
 // tcgen05.mma.cta_group::2 (M=256, N=256, K=64): each CTA loads its own 128
 // rows of A and its own 128 rows of B (half of the tile's N), so per output
-// element each SM streams half the B bytes of the single-CTA 128x256 tile.
-// Scale factors: each CTA holds SFA for its 128 rows and SFB for all 256
-// columns; the leader's scale copiers issue tcgen05.cp.cta_group::2 (each CTA's
-// shared memory into its own TMEM) and its MMA thread issues the pair MMAs.
-// All loads signal the leader's full barrier (.cta_group::2 TMA); MMA
-// completion is multicast to both CTAs' empty / accumulator barriers.  No load
-// uses cluster multicast.
+// element each SM streams half the B bytes of the single-CTA 128x256 tile and
+// its shared memory sees 32 KB of TMA writes and 32 KB of MMA reads per K tile
+// instead of 48 + 48 KB.  Scale factors: each CTA holds SFA for its 128 rows
+// and SFB for all 256 columns in its own TMEM, written by its own four
+// writer warps (tcgen05.st) from its own shared memory.  A and B loads signal
+// the leader's full barrier (.cta_group::2 TMA); the writers of both CTAs
+// arrive on the leader's sf_ready barrier; MMA completion is multicast to
+// both CTAs' empty / accumulator barriers.  No load uses cluster multicast.
 namespace pair {
 constexpr int kStages = 5;
 constexpr int kA = kBM * kBKBytes;       // 16 KB: this CTA's 128 rows of A
@@ -556,7 +709,8 @@ constexpr int kB = 128 * kBKBytes;       // 16 KB: this CTA's 128 rows of B
 constexpr int kSfa = kSfStageBytes;      // 2 KB
 constexpr int kSfb = 2 * kSfStageBytes;  // 4 KB: both 128-row blocks of the tile's N
 constexpr int kStage = kA + kB + kSfa + kSfb;
-constexpr int kTx = 2 * kStage;  // the leader's full barrier counts both CTAs' bytes
+constexpr int kTx = 2 * (kA + kB);  // the leader's full barrier counts both CTAs' A and B bytes
+constexpr int kSfTx = kSfa + kSfb;  // each CTA's own sf_full barrier: its scale runs
 constexpr int kAccCols = 256;
 constexpr int kSfCols = 48;
 constexpr int kTmemCols = 512;
@@ -574,15 +728,6 @@ __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
-__device__ __forceinline__ void tma_load_5d_pair(void* dst, const CUtensorMap* map, uint32_t mbar_cluster, int c2,
-                                                 int c3, int c4, uint64_t hint) {
-  asm volatile(
-      "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(0), "r"(0), "r"(c2), "r"(c3), "r"(c4), "r"(mbar_cluster), "l"(hint)
-      : "memory");
-}
-
 __device__ __forceinline__ void mma_nvf4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                               uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
   asm volatile(
@@ -592,10 +737,6 @@ __device__ __forceinline__ void mma_nvf4_pair(uint32_t d_tmem, uint64_t a_desc, 
           d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
-}
-
-__device__ __forceinline__ void tmem_cp_pair(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
 // Arrive on the barrier at this offset in the CTAs of `mask` when this
@@ -617,6 +758,10 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
                "r"(ncols)
@@ -628,9 +773,8 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                     const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
                      const GemmParams p) {
   using namespace pair;
   constexpr int S = kStages;
@@ -640,10 +784,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* sf_ready = bars + 2 * S;
-  uint64_t* acc_full = bars + 3 * S;
+  uint64_t* sf_full = bars + 3 * S;
+  uint64_t* acc_full = bars + 4 * S;
   uint64_t* acc_empty = acc_full + 1;
-  uint64_t* drain = acc_empty + 1;  // [0] MMA thread, [1..kCopiers] copiers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1 + kCopiers);
+  uint64_t* drain = acc_empty + 1;  // MMA thread
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -657,16 +802,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&sf_ready[s], kCopiers);
+      mbar_init(&sf_ready[s], 2 * kPairCopiers);  // the leader's: both CTAs' writer warps
+      mbar_init(&sf_full[s], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * 128);
-    for (int d = 0; d <= kCopiers; ++d) mbar_init(drain + d, 1);
+    mbar_init(drain, 1);
     fence_barrier_init();
     prefetch_tensormap(&tm_a);
     prefetch_tensormap(&tm_b);
-    prefetch_tensormap(&tm_sfa);
-    prefetch_tensormap(&tm_sfb);
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, kTmemCols);
   tc_fence_before();
@@ -676,6 +820,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sf_col0 = kAccCols;
   if (threadIdx.x == 0) pdl_allow_dependents();
   pdl_wait();
+  TRACE_DECL;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -689,8 +834,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_coords(p, t, mb, nb, l);
         const int arow = mb * 256 + static_cast<int>(rank) * 128;
         const int brow = nb * 256 + static_cast<int>(rank) * 128;
+        const uint8_t* sfa_src = p.sfa + l * p.sfa_lstride + static_cast<int64_t>(arow / 128) * p.K * 8;
+        const uint8_t* sfb_src = p.sfb + l * p.sfb_lstride + static_cast<int64_t>(nb) * 2 * p.K * 8;
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+          if (!TRW(3, mbar_wait(&empty[stage], phase ^ 1))) {
             set_status(p.status, kStatusTimeoutEmpty);
             abort_flag = 1;
             break;
@@ -700,8 +847,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) mbar_arrive_expect_tx(&full[stage], kTx);
           tma_load_3d_pair(st, &tm_a, bar0, kt * kBKBytes, arow, l, pol_a);
           tma_load_3d_pair(st + kA, &tm_b, bar0, kt * kBKBytes, brow, l, pol_b);
-          tma_load_5d_pair(st + kA + kB, &tm_sfa, bar0, kt, arow / 128, l, pol_a);
-          tma_load_5d_pair(st + kA + kB + kSfa, &tm_sfb, bar0, kt, nb * 2, l, pol_b);
+          // Scales into this CTA's own shared memory, on its own barrier: SFA
+          // of its 128 rows, SFB of both 128-row blocks of the tile's N.
+          mbar_arrive_expect_tx(&sf_full[stage], kSfTx);
+          bulk_load(st + kA + kB, sfa_src + kt * kSfStageBytes, kSfStageBytes, &sf_full[stage], pol_a);
+          bulk_load(st + kA + kB + kSfa, sfb_src + kt * kSfStageBytes, kSfStageBytes, &sf_full[stage], pol_b);
+          bulk_load(st + kA + kB + kSfa + kSfStageBytes, sfb_src + static_cast<int64_t>(p.K) * 8 + kt * kSfStageBytes,
+                    kSfStageBytes, &sf_full[stage], pol_b);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -724,7 +876,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&full[stage], phase) || !mbar_wait(&sf_ready[stage], phase)) {
+          if (!TRW(0, mbar_wait(&full[stage], phase)) || !TRW(1, mbar_wait_cluster(&sf_ready[stage], phase))) {
             set_status(p.status, kStatusTimeoutFull);
             abort_flag = 1;
             ok = false;
@@ -752,40 +904,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drain, 0);
     }
   } else if (warp >= 6) {
-    // ------------------------------------------------------------ scale copiers (leader)
-    if (lane == 0 && leader) {
-      const int ci = warp - 6;
-      int stage = 0;
-      uint32_t phase = 0;
-      int total = 0;
-      for (int t = pair_id; t < p.num_tiles; t += npairs) total += KT;
-      for (int i = 0; i < total && !abort_flag; ++i) {
-        if (!mbar_wait(&full[stage], phase)) {
-          set_status(p.status, kStatusTimeoutFull);
-          abort_flag = 1;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t sf = smem_u32(smem + stage * kStage + kA + kB);
-        const uint32_t sfc = tmem_base + sf_col0 + stage * kSfCols;
-        // SFA step kk at column 4*kk; SFB block j of step kk at 16 + 4*(2*kk + j).
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          if (kk % kCopiers == ci) tmem_cp_pair(sfc + 4 * kk, desc_sf_block(sf + kk * kSfBlockBytes));
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            if ((4 + j * 4 + kk) % kCopiers == ci)
-              tmem_cp_pair(sfc + 16 + 4 * (2 * kk + j), desc_sf_block(sf + kSfa + j * kSfStageBytes + kk * kSfBlockBytes));
-        tc_commit_pair(&sf_ready[stage]);
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1;
-        }
+    // ------------------------------------------------------------ scale writers (both CTAs)
+    // Warps 6..9 of each CTA, one per TMEM lane quarter, write the CTA's own
+    // scale runs into its own TMEM with tcgen05.st, in the layout
+    // tcgen05.cp.32x128b.warpx4 would leave (SFA step kk at column 4*kk; SFB
+    // block j of step kk at 16 + 4*(2*kk + j)), then arrive on the leader's
+    // sf_ready[stage], which the leader's MMA thread waits for.
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t ready0 = map_peer(smem_u32(sf_ready), 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    int total = 0;
+    for (int t = pair_id; t < p.num_tiles; t += npairs) total += KT;
+    for (int i = 0; i < total; ++i) {
+      const bool got = TRW(4, mbar_wait(&sf_full[stage], phase));
+      if (!__all_sync(0xffffffffu, got && !abort_flag)) {
+        if (lane == 0 && !got) set_status(p.status, kStatusTimeoutFull);
+        abort_flag = 1;
+        break;
       }
-      tc_commit_pair(drain + 1 + ci);
-      mbar_wait(drain + 1 + ci, 0);
+      const uint8_t* sf = smem + stage * kStage + kA + kB + lane * 16;
+      const uint32_t sfc = tmem_base + lane_base + sf_col0 + stage * kSfCols;
+#pragma unroll
+      for (int r = 0; r < 3; ++r)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint4 v = *reinterpret_cast<const uint4*>(sf + r * kSfStageBytes + kk * kSfBlockBytes);
+          tmem_st_32x32b_x4(sfc + (r == 0 ? 4 * kk : 16 + 4 * (2 * kk + (r - 1))), v);
+        }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      // The stores are complete (tcgen05.wait::st) and ordered before this
+      // signal (tcgen05.fence::before_thread_sync), so a relaxed arrive is
+      // enough; an arrive.release.cluster per stage measured ~1500 cycles
+      // and made this signal the pair kernel's bottleneck.
+      if (lane == 0) mbar_arrive_cluster_relaxed(ready0 + stage * 8);
+      if (++stage == S) {
+        stage = 0;
+        phase ^= 1;
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
@@ -795,7 +953,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = pair_id; t < p.num_tiles; t += npairs) {
       int mb, nb, l;
       tile_coords(p, t, mb, nb, l);
-      if (!__all_sync(0xffffffffu, mbar_wait(acc_full, acc_phase))) {
+      if (!__all_sync(0xffffffffu, TRW(6, mbar_wait(acc_full, acc_phase)))) {
         if (lane == 0) set_status(p.status, kStatusTimeoutAccFull);
         abort_flag = 1;
         break;
@@ -817,6 +975,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+#ifdef NVFP4_TRACE
+  if (warp == 1) TRACE_TOTAL(2);
+  if (warp == 6) TRACE_TOTAL(5);
+  if (warp == 2) TRACE_TOTAL(7);
+  if (warp <= 2 || warp == 6) TRACE_FLUSH();
+#endif
   // The leader's MMAs read both CTAs' shared memory and write both TMEMs:
   // neither CTA frees TMEM or exits before the pair's work has drained.
   tc_fence_before();
@@ -982,6 +1146,10 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
   p.status = g.status;
   p.splits = g.splits > 1 ? g.splits : 1;
   p.num_items = p.num_tiles * p.splits;
+  p.streamk = (!kDual && p.splits == 1 && g.streamk && g.workspace) ? 1 : 0;
+  p.units = static_cast<int64_t>(p.num_tiles) * (g.K / kBK);
+  p.sk_flag = static_cast<int*>(g.workspace);
+  p.sk_partial = p.streamk ? reinterpret_cast<float*>(static_cast<uint8_t*>(g.workspace) + kStreamKFlagBytes) : nullptr;
   // Test hook for the bounded-wait path (tests/test_failure_detection.py):
   // the kernel then reports a pipeline timeout instead of hanging.
   const char* fi = getenv("NVFP4_FAULT_INJECT");
@@ -989,6 +1157,10 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
   // Without split: a persistent grid.  With split K: one CTA per (tile,
   // split), the splits of a tile in one cluster.
   const int grid = p.splits == 1 ? (p.num_items < num_sms ? p.num_items : num_sms) : p.num_items;
+  if (p.streamk && grid * (kBM * BN * 4) + kStreamKFlagBytes > static_cast<int64_t>(g.workspace_bytes)) {
+    *why = "stream-K workspace too small";
+    return cudaErrorInvalidValue;
+  }
   return launch_pdl(gemm_kernel<BN, kDual>, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, stream, p.splits, ta, tb,
                     tb2, p);
 }
@@ -1063,6 +1235,28 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms) {
   }
   pl.splits = splits < 1 ? 1 : splits;
   pl.workspace_bytes = 0;
+  pl.streamk = 0;
+  pl.pair = 0;
+  // Stream-K when whole tiles leave the last wave part-empty: e.g. 224 tiles
+  // on 148 SMs run as two tile-waves (76 SMs busy in the second) against
+  // ceil(224 * KT / 148) K tiles per SM in equal ranges.  Worth it when the
+  // busiest SM's K tiles drop by more than 10%.
+  // 2-CTA pairs (256x256 tiles) whenever the shape allows: per K tile each
+  // SM moves 32 KB through shared memory for TMA writes and 32 KB for MMA
+  // reads instead of 48 + 48 KB with 128x256 tiles (measured +17% on
+  // 1024x7168x16384, +27% on 16384^3).  NVFP4_PAIR=0 keeps 1-CTA tiles.
+  const char* pe = getenv("NVFP4_PAIR");
+  pl.pair = (!dual && pl.bn == 256 && pl.splits == 1 && M % 256 == 0 && !(pe && pe[0] == '0')) ? 1 : 0;
+  const int forced_sk = env_int("NVFP4_STREAMK");  // 1 force on, -1 force off
+  if (!dual && !pl.pair && pl.splits == 1 && tiles > num_sms && forced_sk >= 0) {
+    const int64_t classic = static_cast<int64_t>((tiles + num_sms - 1) / num_sms) * KT;
+    const int64_t units = static_cast<int64_t>(tiles) * KT;
+    const int64_t sk = (units + num_sms - 1) / num_sms + 2;  // +2: partial write / read
+    if (forced_sk == 1 || sk * 10 < classic * 9) {
+      pl.streamk = 1;
+      pl.workspace_bytes = kStreamKFlagBytes + static_cast<size_t>(num_sms) * 128 * pl.bn * 4;
+    }
+  }
   return pl;
 }
 
@@ -1076,7 +1270,7 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(kPairThreads);
     cfg.dynamicSmemBytes = pair::kSmem;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -1093,21 +1287,18 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
     max_pairs[dev] = n;
     attr_done[dev] = true;
   }
-  const uint64_t K2 = g.K / 2, KT = g.K / kBK;
-  CUtensorMap ta, tb, tsfa, tsfb;
-  const uint64_t dsa[5] = {256, 8, KT, static_cast<uint64_t>(g.M / 128), static_cast<uint64_t>(g.L)};
-  const uint64_t ssa[4] = {256, 2048, static_cast<uint64_t>(g.K) * 8, static_cast<uint64_t>(g.sfa_lstride)};
-  const uint32_t bsa[5] = {256, 8, 1, 1, 1};
-  const uint64_t dsb[5] = {256, 8, KT, static_cast<uint64_t>(g.N / 128), static_cast<uint64_t>(g.L)};
-  const uint64_t ssb[4] = {256, 2048, static_cast<uint64_t>(g.K) * 8, static_cast<uint64_t>(g.sfb_lstride)};
-  const uint32_t bsb[5] = {256, 8, 1, 2, 1};
+  const uint64_t K2 = g.K / 2;
+  CUtensorMap ta, tb;
   if (!make_operand_map(&ta, g.a, K2, g.M, g.L, g.a_lstride, 128) ||
-      !make_operand_map(&tb, g.b, K2, g.N, g.L, g.b_lstride, 128) || !make_tma_u8(&tsfa, g.sfa, 5, dsa, ssa, bsa) ||
-      !make_tma_u8(&tsfb, g.sfb, 5, dsb, ssb, bsb)) {
+      !make_operand_map(&tb, g.b, K2, g.N, g.L, g.b_lstride, 128)) {
     *why = "cuTensorMapEncodeTiled failed";
     return cudaErrorInvalidValue;
   }
   GemmParams p{};
+  p.sfa = static_cast<const uint8_t*>(g.sfa);
+  p.sfb = static_cast<const uint8_t*>(g.sfb);
+  p.sfa_lstride = g.sfa_lstride;
+  p.sfb_lstride = g.sfb_lstride;
   p.c = static_cast<__half*>(g.c);
   p.M = g.M;
   p.N = g.N;
@@ -1125,14 +1316,11 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
   int pairs = max_pairs[dev < 64 ? dev : 0];
   if (pairs > p.num_tiles) pairs = p.num_tiles;
   if (pairs < 1) pairs = 1;
-  return launch_pdl(gemm_pair_kernel, dim3(2 * pairs), dim3(kThreads), pair::kSmem, stream, 2, ta, tb, tsfa, tsfb,
-                    p);
+  return launch_pdl(gemm_pair_kernel, dim3(2 * pairs), dim3(kPairThreads), pair::kSmem, stream, 2, ta, tb, p);
 }
 
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {
-  const char* pe = getenv("NVFP4_PAIR");  // "0": keep 1-CTA tiles (comparison / tests)
-  const bool pair_ok = !(pe && pe[0] == '0');
-  if (g.bn == 256 && g.splits == 1 && g.M % 256 == 0 && pair_ok) return launch_pair(g, num_sms, stream, why);
+  if (g.pair) return launch_pair(g, num_sms, stream, why);
   if (g.bn == 256) return launch_impl<256, false>(g, num_sms, stream, why);
   return launch_impl<128, false>(g, num_sms, stream, why);
 }
@@ -1142,3 +1330,11 @@ cudaError_t launch_dual_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream
 }
 
 }  // namespace nvfp4
+
+#ifdef NVFP4_TRACE
+extern "C" __attribute__((visibility("default"))) int nvfp4_dbg_gemm_trace(unsigned long long* host) {
+  if (cudaMemcpyFromSymbol(host, nvfp4::g_gemm_trace, sizeof(nvfp4::g_gemm_trace)) != cudaSuccess) return 1;
+  static unsigned long long zero[1024 * 8];
+  return cudaMemcpyToSymbol(nvfp4::g_gemm_trace, zero, sizeof(zero)) != cudaSuccess;
+}
+#endif

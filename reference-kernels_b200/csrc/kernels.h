@@ -82,12 +82,16 @@ struct GemmArgs {
   int64_t sfa_lstride, sfb_lstride, sfb2_lstride;  // bytes
   int64_t ldc, c_lstride;                          // elements
   int* status;                                     // device status word (bounded-wait timeouts)
-  int bn, splits;                                  // from gemm_plan
+  int bn, splits, streamk, pair;                   // from gemm_plan
+  void* workspace;                                 // stream-K partials + flags (zeroed once; left zeroed)
+  size_t workspace_bytes;
 };
 struct GemmPlan {
   int bn;      // N tile: 128 or 256
   int splits;  // K splits per tile
-  size_t workspace_bytes;  // always 0 (split K reduces on chip)
+  int streamk;  // 1: stream-K ranges over (tile, K tile) units (plain GEMM, tiles > SMs)
+  int pair;     // 1: 2-CTA kernel, 256x256 tiles (plain GEMM, M % 256 == 0, N % 256 == 0, no split)
+  size_t workspace_bytes;  // stream-K partial slots + flags; 0 otherwise (split K reduces on chip)
 };
 GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms);
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why);

@@ -159,3 +159,28 @@ def test_pair_gemm_matches_single_cta_and_oracle(m, n, k, l, monkeypatch):
     assert_match(pair1, single, f"pair vs single {m}x{n}x{k}x{l}")
     if m * n * k <= 768 * 1024 * 2048:
         assert_match(pair1, oracle_ref("gemm", data), f"pair vs oracle {m}x{n}x{k}x{l}")
+
+
+@pytest.mark.parametrize("m,n,k,l", [
+    (1664, 3072, 512, 1),    # 156 tiles of 128x256, ~2.1 K tiles per CTA: tiles cut three ways
+    (1280, 2176, 1024, 1),   # N % 256 != 0: 128x128 tiles, 170 of them
+    (1024, 7168, 2048, 1),   # benchmark config's M, N (224 tiles), short K
+    (768, 3328, 1280, 2),    # L = 2: ranges cross batch boundaries
+])
+def test_stream_k_gemm(m, n, k, l, monkeypatch):
+    """Stream-K GEMM (equal (tile, K tile) ranges per CTA, partial tiles
+    combined through the workspace) against the oracle / _scaled_mm, the
+    classic tile-per-CTA path, and itself (bit-identical on repeat)."""
+    data = inputs.baseline_input("gemm", m, k, l, 33, n=n)
+    monkeypatch.setenv("NVFP4_PAIR", "0")  # stream-K runs on the 1-CTA kernel
+    monkeypatch.setenv("NVFP4_STREAMK", "-1")
+    classic = run("gemm", data).clone()
+    monkeypatch.setenv("NVFP4_STREAMK", "1")
+    sk1 = run("gemm", data).clone()
+    sk2 = run("gemm", data).clone()
+    assert torch.equal(sk1, sk2)
+    assert_match(sk1, classic, f"stream-K vs classic {m}x{n}x{k}x{l}")
+    if m * n * k * l <= 1664 * 3072 * 512:
+        assert_match(sk1, oracle_ref("gemm", data), f"stream-K vs oracle {m}x{n}x{k}x{l}")
+    else:
+        assert_match(sk1, scaled_mm_ref("gemm", data), f"stream-K vs _scaled_mm {m}x{n}x{k}x{l}")
