@@ -194,6 +194,23 @@ static int check_gemm_common(const char* name, const void* a, const void* b, con
   return NVFP4_OK;
 }
 
+// Copies a GEMM plan into the launch arguments and attaches the stream-K
+// workspace when the plan needs one.
+static int apply_plan(const char* who, int dev, const GemmPlan& pl, GemmArgs& g, void* stream) {
+  g.bn = pl.bn;
+  g.splits = pl.splits;
+  g.streamk = pl.streamk;
+  g.streamk_pure = pl.streamk_pure;
+  g.pair = pl.pair;
+  if (pl.workspace_bytes) {
+    cudaError_t we;
+    g.workspace = workspace_for(kWsGemm, dev, pl.workspace_bytes, static_cast<cudaStream_t>(stream), &we);
+    if (!g.workspace) return fail(NVFP4_ERR_CUDA, "%s: workspace: %s", who, cudaGetErrorString(we));
+    g.workspace_bytes = pl.workspace_bytes;
+  }
+  return NVFP4_OK;
+}
+
 NVFP4_API int nvfp4_gemm(const void* a, const void* b, const void* sfa_blk, const void* sfb_blk, void* c, int M, int N, int K,
                int L, int64_t a_lstride, int64_t b_lstride, int64_t sfa_lstride, int64_t sfb_lstride, int64_t ldc,
                int64_t c_lstride, void* stream) {
@@ -224,16 +241,8 @@ NVFP4_API int nvfp4_gemm(const void* a, const void* b, const void* sfa_blk, cons
   g.c_lstride = c_lstride;
   g.status = status_ptr(dev);
   const GemmPlan pl = gemm_plan(M, N, K, L, false, num_sms_of(dev));
-  g.bn = pl.bn;
-  g.splits = pl.splits;
-  g.streamk = pl.streamk;
-  g.pair = pl.pair;
-  if (pl.workspace_bytes) {
-    cudaError_t we;
-    g.workspace = workspace_for(kWsGemm, dev, pl.workspace_bytes, static_cast<cudaStream_t>(stream), &we);
-    if (!g.workspace) return fail(NVFP4_ERR_CUDA, "nvfp4_gemm: workspace: %s", cudaGetErrorString(we));
-    g.workspace_bytes = pl.workspace_bytes;
-  }
+  rc = apply_plan("nvfp4_gemm", dev, pl, g, stream);
+  if (rc) return rc;
   const char* why = nullptr;
   cudaError_t e = launch_gemm(g, num_sms_of(dev), static_cast<cudaStream_t>(stream), &why);
   if (e != cudaSuccess)
@@ -274,8 +283,8 @@ NVFP4_API int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, con
   g.c_lstride = c_lstride;
   g.status = status_ptr(dev);
   const GemmPlan pl = gemm_plan(M, N, K, L, true, num_sms_of(dev));
-  g.bn = pl.bn;
-  g.splits = pl.splits;
+  rc = apply_plan("nvfp4_dual_gemm", dev, pl, g, stream);
+  if (rc) return rc;
   const char* why = nullptr;
   cudaError_t e = launch_dual_gemm(g, num_sms_of(dev), static_cast<cudaStream_t>(stream), &why);
   if (e != cudaSuccess)

@@ -43,7 +43,17 @@ namespace nvfp4 {
 // free stage, 4 scale writer waiting for a stage, 5 scale writer total,
 // 6 epilogue waiting for an accumulator, 7 epilogue total (SM cycles).
 #ifdef NVFP4_TRACE
-__device__ unsigned long long g_gemm_trace[1024 * 8];
+__device__ unsigned long long g_gemm_trace[1024 * 32];
+// Slots 8.. hold %globaltimer stamps: 8 kernel entry, 9 after setup and the
+// PDL wait, 10 last accumulator handed to the epilogue, 11 epilogue done,
+// 12 kernel exit.
+#define TRACE_STAMP(slot) g_gemm_trace[blockIdx.x * 32 + (slot)] = global_timer_ns()
+// Slot 13: SM cycles the MMA thread spends issuing (MMAs + commit, after its waits).
+// Slots 14, 15: clock64 of thread 0 at the stamps of slots 9 and 12 (SM MHz).
+#define TRACE_CLOCK(slot) \
+  if (threadIdx.x == 0) g_gemm_trace[blockIdx.x * 32 + (slot)] = clock64()
+#define TRACE_ISSUE_BEGIN const long long _ti0 = clock64()
+#define TRACE_ISSUE_END trace[13] += clock64() - _ti0
 #define TRW(slot, expr)                      \
   ({                                         \
     const long long _t0 = clock64();         \
@@ -51,19 +61,23 @@ __device__ unsigned long long g_gemm_trace[1024 * 8];
     trace[slot] += clock64() - _t0;          \
     _r;                                      \
   })
-#define TRACE_DECL unsigned long long trace[8] = {0, 0, 0, 0, 0, 0, 0, 0}; const long long trace_t0 = clock64()
+#define TRACE_DECL unsigned long long trace[16] = {}; const long long trace_t0 = clock64()
 #define TRACE_TOTAL(slot) trace[slot] = clock64() - trace_t0
 #define TRACE_FLUSH()                                                             \
   do {                                                                            \
     if (lane == 0)                                                                \
-      for (int _i = 0; _i < 8; ++_i)                                              \
-        if (trace[_i]) g_gemm_trace[blockIdx.x * 8 + _i] = trace[_i];             \
+      for (int _i = 0; _i < 16; ++_i)                                             \
+        if (trace[_i]) g_gemm_trace[blockIdx.x * 32 + _i] = trace[_i];             \
   } while (0)
 #else
 #define TRW(slot, expr) (expr)
 #define TRACE_DECL
 #define TRACE_TOTAL(slot)
 #define TRACE_FLUSH()
+#define TRACE_STAMP(slot)
+#define TRACE_ISSUE_BEGIN
+#define TRACE_ISSUE_END
+#define TRACE_CLOCK(slot)
 #endif
 
 constexpr int kBM = 128;
@@ -94,7 +108,8 @@ struct GemmConfig {
   static constexpr int kSfCols = 16 * kSfOps;                         // TMEM columns of scales per stage
   static constexpr int kTmemCols = 512;
   static_assert(kAccBufs * kAccCols + kStages * kSfCols <= kTmemCols, "TMEM budget");
-  static constexpr int kTxBytes = kStageBytes + kSfOps * kSfStageBytes;
+  static constexpr int kTxBytes = kStageBytes;                 // full[]: A and B tiles
+  static constexpr int kSfTxBytes = kSfOps * kSfStageBytes;     // sf_full[]: the stage's scale runs
   static constexpr int kSmemBytes =
       1024 /*align slack*/ + kStages * (kStageBytes + kSfOps * kSfStageBytes) + 256 /*barriers*/;
 };
@@ -114,14 +129,21 @@ struct GemmParams {
                 // With splits > 1 the kernel is launched with clusters of
                 // `splits` CTAs, one item per CTA, cluster = tile.
   int num_items;
+  int prefetch;  // K tiles ahead to prefetch B into L2 (0 = off)
   // Stream-K (splits == 1 only): the tiles x K-tiles "units", in tile-major
   // order, are cut into gridDim.x equal contiguous ranges, one per CTA.  A CTA
   // whose range starts inside a tile (its first segment) writes that partial
   // tile, fp32, to slot blockIdx.x of sk_partial and raises sk_flag[blockIdx.x];
   // the CTA holding the tile's first K tiles (its last segment) adds the
   // partials of the following CTAs, in CTA order, and writes C.
+  // Hybrid form: tiles [0, dp_tiles) are whole work items dealt round-robin
+  // (dp_tiles a multiple of the worker count, the full waves), and only the
+  // remaining tiles' units are cut into the equal ranges, so the full waves
+  // keep the classic lockstep order over K (the tiles sharing an A or B slice
+  // read it at about the same time, from L2).
   int streamk;
-  int64_t units;
+  int dp_tiles;
+  int64_t units;  // units of the split tiles [dp_tiles, num_tiles)
   float* sk_partial;  // gridDim.x slots of kBM x BN floats
   int* sk_flag;       // gridDim.x flags, 0 between launches
   int* status;
@@ -133,26 +155,36 @@ __device__ __forceinline__ void split_range(int KT, int splits, int s, int& k0, 
   k1 = ((s + 1) * KT) / splits;
 }
 
-// First unit of CTA b's stream-K range.
-__device__ __forceinline__ int64_t sk_begin(const GemmParams& p, int b) {
-  return (static_cast<int64_t>(b) * p.units) / gridDim.x;
+// First unit of worker b's stream-K range (nw workers: CTAs, or CTA pairs).
+__device__ __forceinline__ int64_t sk_begin(const GemmParams& p, int b, int nw) {
+  return (static_cast<int64_t>(b) * p.units) / nw;
 }
 
-// The work items of this CTA, in order: (tile, K-tile range).  Every warp role
-// walks the same sequence.
+// The work items of worker w of nw (a CTA, or a CTA pair), in order: (tile,
+// K-tile range).  Every warp role walks the same sequence.
 struct WorkIter {
   int64_t u, u_end;
-  int it;
-  __device__ __forceinline__ explicit WorkIter(const GemmParams& p) {
-    it = blockIdx.x;
-    u = p.streamk ? sk_begin(p, blockIdx.x) : 0;
-    u_end = p.streamk ? sk_begin(p, blockIdx.x + 1) : 0;
+  int it, nw, dp_t;
+  __device__ __forceinline__ WorkIter(const GemmParams& p, int w, int nw_) {
+    it = w;
+    nw = nw_;
+    u = p.streamk ? sk_begin(p, w, nw) : 0;
+    u_end = p.streamk ? sk_begin(p, w + 1, nw) : 0;
+    dp_t = (p.streamk && w < p.dp_tiles) ? w : -1;  // whole tiles first
   }
   __device__ __forceinline__ bool next(const GemmParams& p, int KT, int& t, int& k0, int& k1) {
     if (p.streamk) {
+      if (dp_t >= 0) {
+        t = dp_t;
+        k0 = 0;
+        k1 = KT;
+        dp_t = (dp_t + nw < p.dp_tiles) ? dp_t + nw : -1;
+        return true;
+      }
       if (u >= u_end) return false;
-      t = static_cast<int>(u / KT);
-      k0 = static_cast<int>(u - static_cast<int64_t>(t) * KT);
+      const int ts = static_cast<int>(u / KT);
+      t = p.dp_tiles + ts;
+      k0 = static_cast<int>(u - static_cast<int64_t>(ts) * KT);
       const int64_t rem = u_end - u;
       k1 = (KT - k0 > rem) ? k0 + static_cast<int>(rem) : KT;
       u += k1 - k0;
@@ -161,10 +193,21 @@ struct WorkIter {
     if (it >= p.num_items) return false;
     t = it / p.splits;
     split_range(KT, p.splits, it - t * p.splits, k0, k1);
-    it += gridDim.x;
+    it += nw;
     return true;
   }
 };
+
+// Whether worker c has a non-empty stream-K range (ranges are empty when the
+// split tiles have fewer units than there are workers).
+__device__ __forceinline__ bool sk_has_range(const GemmParams& p, int c, int nw) {
+  return sk_begin(p, c, nw) < sk_begin(p, c + 1, nw);
+}
+
+// End (exclusive, in stream-K units) of split tile t.
+__device__ __forceinline__ int64_t sk_tile_end(const GemmParams& p, int t, int KT) {
+  return static_cast<int64_t>(t - p.dp_tiles + 1) * KT;
+}
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -258,6 +301,7 @@ template <int BN, bool kDual>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_b2, const GemmParams p) {
+  if (threadIdx.x == 0) TRACE_STAMP(8);
   using Cfg = GemmConfig<BN, kDual>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -268,7 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* sf_ready = bars + 2 * S;
-  uint64_t* acc_full = bars + 3 * S;
+  uint64_t* sf_full = bars + 3 * S;  // the stage's scale runs landed (before its A/B tiles, usually)
+  uint64_t* acc_full = bars + 4 * S;
   uint64_t* acc_empty = acc_full + Cfg::kAccBufs;
   uint64_t* drain = acc_empty + Cfg::kAccBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -283,6 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
       mbar_init(&sf_ready[s], kCopiers);
+      mbar_init(&sf_full[s], 1);
     }
     for (int b = 0; b < Cfg::kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -303,6 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) pdl_allow_dependents();
   pdl_wait();
   TRACE_DECL;
+  if (threadIdx.x == 0) TRACE_STAMP(9);
+  TRACE_CLOCK(14);
   bool split_ready = false;  // epilogue threads: this CTA's split partial is in TMEM
 
   if (warp == 0) {
@@ -312,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_b = policy_evict_first();
       int stage = 0;
       uint32_t phase = 0;
-      WorkIter wi(p);
+      WorkIter wi(p, blockIdx.x, gridDim.x);
       int t, k0, k1, item = 0;
       for (; !abort_flag && wi.next(p, KT, t, k0, k1); ++item) {
         int mb, nb, l;
@@ -329,22 +377,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* st = tiles + stage * Cfg::kStageBytes;
           uint8_t* sf = sfbuf + stage * Cfg::kSfOps * kSfStageBytes;
+          // Scales first, on their own barrier: the writers can put them in
+          // TMEM while the larger A/B tiles are still arriving.
+          mbar_arrive_expect_tx(&sf_full[stage], Cfg::kSfTxBytes);
+          bulk_load(sf, sfa_src + kt * kSfStageBytes, kSfStageBytes, &sf_full[stage], pol_a);
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j)
+            bulk_load(sf + (1 + j) * kSfStageBytes, sfb_src + static_cast<int64_t>(j) * p.K * 8 + kt * kSfStageBytes,
+                      kSfStageBytes, &sf_full[stage], pol_b);
+          if (kDual) {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              bulk_load(sf + (1 + BN / 128 + j) * kSfStageBytes,
+                        sfb2_src + static_cast<int64_t>(j) * p.K * 8 + kt * kSfStageBytes, kSfStageBytes,
+                        &sf_full[stage], pol_b);
+          }
           mbar_arrive_expect_tx(&full[stage], Cfg::kTxBytes);
           if (!(p.inject && blockIdx.x == 0 && item == 0 && kt == k0))
             tma_load_3d(st, &tm_a, &full[stage], kt * kBKBytes, mb * kBM, l, pol_a);
           tma_load_3d(st + Cfg::kABytes, &tm_b, &full[stage], kt * kBKBytes, nb * BN, l, pol_b);
           if (kDual) tma_load_3d(st + Cfg::kABytes + Cfg::kBBytes, &tm_b2, &full[stage], kt * kBKBytes, nb * BN, l, pol_b);
-          bulk_load(sf, sfa_src + kt * kSfStageBytes, kSfStageBytes, &full[stage], pol_a);
-#pragma unroll
-          for (int j = 0; j < BN / 128; ++j)
-            bulk_load(sf + (1 + j) * kSfStageBytes, sfb_src + static_cast<int64_t>(j) * p.K * 8 + kt * kSfStageBytes,
-                      kSfStageBytes, &full[stage], pol_b);
-          if (kDual) {
-#pragma unroll
-            for (int j = 0; j < BN / 128; ++j)
-              bulk_load(sf + (1 + BN / 128 + j) * kSfStageBytes,
-                        sfb2_src + static_cast<int64_t>(j) * p.K * 8 + kt * kSfStageBytes, kSfStageBytes, &full[stage],
-                        pol_b);
+          // L2 prefetch of the B tiles p.prefetch K tiles ahead (beyond the
+          // shared-memory ring): more DRAM requests in flight for shapes that
+          // stream B from DRAM.
+          if (p.prefetch && kt + p.prefetch < k1) {
+            tma_prefetch_3d(&tm_b, (kt + p.prefetch) * kBKBytes, nb * BN, l);
+            if (kDual) tma_prefetch_3d(&tm_b2, (kt + p.prefetch) * kBKBytes, nb * BN, l);
           }
           if (++stage == S) {
             stage = 0;
@@ -363,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      WorkIter wi(p);
+      WorkIter wi(p, blockIdx.x, gridDim.x);
       int t, k0, k1;
       while (!abort_flag && wi.next(p, KT, t, k0, k1)) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1)) {
@@ -382,6 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          TRACE_ISSUE_BEGIN;
           const uint32_t st = smem_u32(tiles + stage * Cfg::kStageBytes);
           const uint32_t sfc = tmem_base + sf_col0 + stage * Cfg::kSfCols;
 #pragma unroll
@@ -399,6 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           tc_commit(&empty[stage]);
+          TRACE_ISSUE_END;
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -406,6 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         tc_commit(&acc_full[acc]);
+        TRACE_STAMP(10);
         if (++acc == Cfg::kAccBufs) {
           acc = 0;
           acc_phase ^= 1;
@@ -434,12 +495,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     int total = 0;
     {
-      WorkIter wi(p);
+      WorkIter wi(p, blockIdx.x, gridDim.x);
       int t, k0, k1;
       while (wi.next(p, KT, t, k0, k1)) total += k1 - k0;
     }
     for (int i = 0; i < total; ++i) {
-      const bool got = TRW(4, mbar_wait(&full[stage], phase));
+      const bool got = TRW(4, mbar_wait(&sf_full[stage], phase));
       if (!__all_sync(0xffffffffu, got && !abort_flag)) {
         if (lane == 0 && !got) set_status(p.status, kStatusTimeoutFull);
         abort_flag = 1;
@@ -474,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool split = p.splits > 1;
-    WorkIter wi(p);
+    WorkIter wi(p, blockIdx.x, gridDim.x);
     int t, k0, k1;
     while (wi.next(p, KT, t, k0, k1)) {
       int mb, nb, l;
@@ -521,11 +582,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // following CTAs [blockIdx.x + 1, c_end) as their first segments.
         int c_end = blockIdx.x + 1;
         if (p.streamk && k1 < KT) {
-          const int64_t tile_end = static_cast<int64_t>(t + 1) * KT;
-          while (c_end < static_cast<int>(gridDim.x) && sk_begin(p, c_end) < tile_end) ++c_end;
+          const int64_t tile_end = sk_tile_end(p, t, KT);
+          while (c_end < static_cast<int>(gridDim.x) && sk_begin(p, c_end, gridDim.x) < tile_end) ++c_end;
           bool ok = true;
           if (threadIdx.x == 64) {
-            for (int c = blockIdx.x + 1; c < c_end && ok; ++c) ok = flag_wait(p.sk_flag + c);
+            for (int c = blockIdx.x + 1; c < c_end && ok; ++c)
+              if (sk_has_range(p, c, gridDim.x)) ok = flag_wait(p.sk_flag + c);
             if (ok)
               for (int c = blockIdx.x + 1; c < c_end; ++c) p.sk_flag[c] = 0;  // ready for the next launch
             else
@@ -552,6 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Own partial first, then the contributors' in CTA order: the
             // same order on every call with the same grid.
             for (int c = blockIdx.x + 1; c < c_end; ++c) {
+              if (!sk_has_range(p, c, gridDim.x)) continue;
               const float4* src = reinterpret_cast<const float4*>(p.sk_partial) +
                                   static_cast<int64_t>(c) * (kBM * BN / 4) + (c0 / 32) * 8 * kBM + rloc;
 #pragma unroll
@@ -676,6 +739,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
 #ifdef NVFP4_TRACE
+  if (threadIdx.x == 64) TRACE_STAMP(11);
   if (warp == 1) TRACE_TOTAL(2);
   if (warp == 6) TRACE_TOTAL(5);
   if (warp == 2) TRACE_TOTAL(7);
@@ -688,6 +752,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
+  if (threadIdx.x == 0) TRACE_STAMP(12);
+  TRACE_CLOCK(15);
 }
 
 // ------------------------------------------------------------------ 2-CTA GEMM
@@ -716,6 +782,10 @@ constexpr int kSfCols = 48;
 constexpr int kTmemCols = 512;
 static_assert(kAccCols + kStages * kSfCols <= kTmemCols, "TMEM budget");
 static_assert(kStage % 1024 == 0, "stage alignment");
+constexpr int kFixBufs = 8;          // stream-K finaliser ring: 8 x 16 KB in the stage area
+constexpr int kFixChunk = 16 * 1024;  // one (contributor, 32-column group) of a partial slot
+constexpr int kMaxContrib = 16;       // contributors per finalised tile
+static_assert(kFixBufs * kFixChunk <= kStages * kStage, "fix-up ring fits in the stage area");
 constexpr int kSmem = 1024 + kStages * kStage + 256;
 }  // namespace pair
 
@@ -773,9 +843,15 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// kDual: the dual GEMM on 256 x (128 B1 + 128 B2) tiles: CTA 0 loads the B1
+// tile and CTA 1 the B2 tile, which together form the N=256 operand, so the
+// accumulator row of either CTA holds A.B1 in columns [0,128) and A.B2 in
+// [128,256) and the SiLU gate is applied per CTA.
+template <bool kDual>
 __global__ void __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                     const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tm_b2, const GemmParams p) {
+  if (threadIdx.x == 0) TRACE_STAMP(8);
   using namespace pair;
   constexpr int S = kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -788,7 +864,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* acc_full = bars + 4 * S;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drain = acc_empty + 1;  // MMA thread
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* fix_full = drain + 1;   // stream-K finaliser: kFixBufs partial-chunk buffers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fix_full + kFixBufs);
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -808,9 +885,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * 128);
     mbar_init(drain, 1);
+    for (int i = 0; i < kFixBufs; ++i) mbar_init(&fix_full[i], 1);
     fence_barrier_init();
     prefetch_tensormap(&tm_a);
-    prefetch_tensormap(&tm_b);
+    prefetch_tensormap(kDual && rank ? &tm_b2 : &tm_b);
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, kTmemCols);
   tc_fence_before();
@@ -821,6 +899,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (threadIdx.x == 0) pdl_allow_dependents();
   pdl_wait();
   TRACE_DECL;
+  if (threadIdx.x == 0) TRACE_STAMP(9);
+  TRACE_CLOCK(14);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -829,14 +909,21 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const uint64_t pol_b = policy_evict_first();
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = pair_id; t < p.num_tiles && !abort_flag; t += npairs) {
+      WorkIter wi(p, pair_id, npairs);
+      int t, k0, k1;
+      while (!abort_flag && wi.next(p, KT, t, k0, k1)) {
         int mb, nb, l;
         tile_coords(p, t, mb, nb, l);
         const int arow = mb * 256 + static_cast<int>(rank) * 128;
-        const int brow = nb * 256 + static_cast<int>(rank) * 128;
+        const int brow = kDual ? nb * 128 : nb * 256 + static_cast<int>(rank) * 128;
+        const CUtensorMap* bmap = (kDual && rank) ? &tm_b2 : &tm_b;
         const uint8_t* sfa_src = p.sfa + l * p.sfa_lstride + static_cast<int64_t>(arow / 128) * p.K * 8;
-        const uint8_t* sfb_src = p.sfb + l * p.sfb_lstride + static_cast<int64_t>(nb) * 2 * p.K * 8;
-        for (int kt = 0; kt < KT; ++kt) {
+        // SFB blocks 0 and 1 of the N=256 operand: B rows [0,128), [128,256)
+        // of the tile (dual: the B1 and the B2 tile).
+        const uint8_t* sfb_src0 = p.sfb + l * p.sfb_lstride + static_cast<int64_t>(kDual ? nb : 2 * nb) * p.K * 8;
+        const uint8_t* sfb_src1 = kDual ? p.sfb2 + l * p.sfb2_lstride + static_cast<int64_t>(nb) * p.K * 8
+                                        : sfb_src0 + static_cast<int64_t>(p.K) * 8;
+        for (int kt = k0; kt < k1; ++kt) {
           if (!TRW(3, mbar_wait(&empty[stage], phase ^ 1))) {
             set_status(p.status, kStatusTimeoutEmpty);
             abort_flag = 1;
@@ -846,14 +933,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           const uint32_t bar0 = map_peer(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], kTx);
           tma_load_3d_pair(st, &tm_a, bar0, kt * kBKBytes, arow, l, pol_a);
-          tma_load_3d_pair(st + kA, &tm_b, bar0, kt * kBKBytes, brow, l, pol_b);
+          tma_load_3d_pair(st + kA, bmap, bar0, kt * kBKBytes, brow, l, pol_b);
           // Scales into this CTA's own shared memory, on its own barrier: SFA
           // of its 128 rows, SFB of both 128-row blocks of the tile's N.
           mbar_arrive_expect_tx(&sf_full[stage], kSfTx);
           bulk_load(st + kA + kB, sfa_src + kt * kSfStageBytes, kSfStageBytes, &sf_full[stage], pol_a);
-          bulk_load(st + kA + kB + kSfa, sfb_src + kt * kSfStageBytes, kSfStageBytes, &sf_full[stage], pol_b);
-          bulk_load(st + kA + kB + kSfa + kSfStageBytes, sfb_src + static_cast<int64_t>(p.K) * 8 + kt * kSfStageBytes,
-                    kSfStageBytes, &sf_full[stage], pol_b);
+          bulk_load(st + kA + kB + kSfa, sfb_src0 + kt * kSfStageBytes, kSfStageBytes, &sf_full[stage], pol_b);
+          bulk_load(st + kA + kB + kSfa + kSfStageBytes, sfb_src1 + kt * kSfStageBytes, kSfStageBytes,
+                    &sf_full[stage], pol_b);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -868,14 +955,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       int stage = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int t = pair_id; t < p.num_tiles && !abort_flag && ok; t += npairs) {
+      WorkIter wi(p, pair_id, npairs);
+      int t, k0, k1;
+      while (!abort_flag && ok && wi.next(p, KT, t, k0, k1)) {
         if (!mbar_wait(acc_empty, acc_phase ^ 1)) {
           set_status(p.status, kStatusTimeoutAccEmpty);
           abort_flag = 1;
           break;
         }
         tc_fence_after();
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = k0; kt < k1; ++kt) {
           if (!TRW(0, mbar_wait(&full[stage], phase)) || !TRW(1, mbar_wait_cluster(&sf_ready[stage], phase))) {
             set_status(p.status, kStatusTimeoutFull);
             abort_flag = 1;
@@ -889,7 +978,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           for (int kk = 0; kk < kBK / kMmaK; ++kk)
             mma_nvf4_pair(tmem_base, desc_kmajor_sw128(st + kk * (kMmaK / 2)),
                           desc_kmajor_sw128(st + kA + kk * (kMmaK / 2)), idesc, sfc + 4 * kk, sfc + 16 + 8 * kk,
-                          (kt | kk) != 0 ? 1u : 0u);
+                          (kt != k0 || kk != 0) ? 1u : 0u);
           tc_commit_pair_mc(&empty[stage], 0x3);
           if (++stage == S) {
             stage = 0;
@@ -898,6 +987,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
         if (!ok) break;
         tc_commit_pair_mc(acc_full, 0x3);
+        TRACE_STAMP(10);
         acc_phase ^= 1;
       }
       tc_commit_pair(drain);
@@ -915,7 +1005,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     int total = 0;
-    for (int t = pair_id; t < p.num_tiles; t += npairs) total += KT;
+    {
+      WorkIter wi(p, pair_id, npairs);
+      int t, k0, k1;
+      while (wi.next(p, KT, t, k0, k1)) total += k1 - k0;
+    }
     for (int i = 0; i < total; ++i) {
       const bool got = TRW(4, mbar_wait(&sf_full[stage], phase));
       if (!__all_sync(0xffffffffu, got && !abort_flag)) {
@@ -950,7 +1044,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int q = warp & 3;
     const uint32_t acc_empty0 = map_peer(smem_u32(acc_empty), 0);
     uint32_t acc_phase = 0;
-    for (int t = pair_id; t < p.num_tiles; t += npairs) {
+    WorkIter wi(p, pair_id, npairs);
+    int t, k0, k1;
+    // Stream-K slots and flags are per CTA: worker (pair) w, rank r -> 2w + r.
+    const int my_slot = pair_id * 2 + static_cast<int>(rank);
+    while (wi.next(p, KT, t, k0, k1)) {
       int mb, nb, l;
       tile_coords(p, t, mb, nb, l);
       if (!__all_sync(0xffffffffu, TRW(6, mbar_wait(acc_full, acc_phase)))) {
@@ -959,23 +1057,129 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         break;
       }
       tc_fence_after();
-      const int row = mb * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
-      __half* crow = p.c + l * p.c_lstride + static_cast<int64_t>(row) * p.ldc + static_cast<int64_t>(nb) * 256;
+      const int rloc = q * 32 + lane;
+      const int row = mb * 256 + static_cast<int>(rank) * 128 + rloc;
+      __half* crow = p.c + l * p.c_lstride + static_cast<int64_t>(row) * p.ldc + static_cast<int64_t>(nb) * (kDual ? 128 : 256);
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+      if (p.streamk && k0 > 0) {
+        // Contributor: this CTA's 128 rows of the partial tile to its slot
+        // ([column group][float4 index][row][4] floats), then its flag.
+        float4* dst = reinterpret_cast<float4*>(p.sk_partial) + static_cast<int64_t>(my_slot) * (128 * 256 / 4) + rloc;
 #pragma unroll 1
-      for (int c0 = 0; c0 < 256; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tacc + c0, r);
-        tmem_wait_ld();
-        store_half_row32(crow + c0, r);
+        for (int c0 = 0; c0 < 256; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tacc + c0, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[((c0 / 32) * 8 + i) * 128] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                                         __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+        }
+        tc_fence_before();
+        mbar_arrive_cluster_relaxed(acc_empty0);
+        epi_bar();
+        if (threadIdx.x == 64) {
+          __threadfence();
+          st_release_gpu(p.sk_flag + my_slot, 1);
+        }
+      } else {
+        // Whole tile, or the finaliser of a tile whose K tiles [k1, KT)
+        // the following pairs [pair_id + 1, c_end) computed.
+        int c_end = pair_id + 1;
+        if (p.streamk && k1 < KT) {
+          const int64_t tile_end = sk_tile_end(p, t, KT);
+          while (c_end < npairs && sk_begin(p, c_end, npairs) < tile_end) ++c_end;
+          bool ok = true;
+          if (threadIdx.x == 64) {
+            for (int c = pair_id + 1; c < c_end && ok; ++c)
+              if (sk_has_range(p, c, npairs)) ok = flag_wait(p.sk_flag + 2 * c + rank);
+            if (ok)
+              for (int c = pair_id + 1; c < c_end; ++c) p.sk_flag[2 * c + rank] = 0;  // ready for the next launch
+            else
+              set_status(p.status, kStatusTimeoutPeer);
+          }
+          if (!epi_all(ok)) {
+            abort_flag = 1;
+            break;
+          }
+          if (threadIdx.x == 64) TRACE_STAMP(16);
+        }
+        // The contributors' partials are streamed into shared memory (free
+        // now: this is the CTA's last segment and its MMAs are complete) by
+        // bulk copies of 16 KB chunks, one (contributor, 32-column group)
+        // each, through a ring of kFixBufs buffers; plain loads of the same
+        // data from L2 were latency-bound (~17 GB/s per SM).
+        int contrib[kMaxContrib];
+        int nc = 0;
+        for (int c = pair_id + 1; c < c_end; ++c)
+          if (sk_has_range(p, c, npairs) && nc < kMaxContrib) contrib[nc++] = c;
+        constexpr int kHalves = kDual ? 2 : 1;  // accumulator groups per output chunk
+        constexpr int kOut = kDual ? 4 : 8;     // 32-column output chunks
+        const int nchunks = kOut * kHalves * nc;
+        auto issue = [&](int q) {  // chunk q -> ring buffer q % kFixBufs
+          const int j = q % nc, h = (q / nc) % kHalves, o = q / (nc * kHalves);
+          const int g = o + h * 4;
+          const uint8_t* src = reinterpret_cast<const uint8_t*>(p.sk_partial) +
+                               (static_cast<int64_t>(2 * contrib[j] + rank) * 8 + g) * kFixChunk;
+          mbar_arrive_expect_tx(&fix_full[q % kFixBufs], kFixChunk);
+          bulk_load(smem + (q % kFixBufs) * kFixChunk, src, kFixChunk, &fix_full[q % kFixBufs],
+                    policy_evict_first());
+        };
+        if (threadIdx.x == 64)
+          for (int q = 0; q < nchunks && q < kFixBufs; ++q) issue(q);
+        bool fix_ok = true;
+        int q = 0;
+#pragma unroll 1
+        for (int o = 0; o < kOut; ++o) {
+          uint32_t r[kHalves][32];
+#pragma unroll
+          for (int h = 0; h < kHalves; ++h) {
+            tmem_ld_32x32b_x32(tacc + o * 32 + h * 128, r[h]);
+            tmem_wait_ld();
+            for (int j = 0; j < nc; ++j, ++q) {
+              fix_ok &= mbar_wait(&fix_full[q % kFixBufs], (q / kFixBufs) & 1);
+#ifdef NVFP4_TRACE
+              if (threadIdx.x == 64 && q < 12) TRACE_STAMP(18 + q);
+#endif
+              const float4* buf = reinterpret_cast<const float4*>(smem + (q % kFixBufs) * kFixChunk) + rloc;
+              float4 v[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) v[i] = buf[i * 128];
+              // Every thread has read buffer q: refill it with chunk q + kFixBufs.
+              epi_bar();
+              if (threadIdx.x == 64 && q + kFixBufs < nchunks) {
+                fence_proxy_async_smem();
+                issue(q + kFixBufs);
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                r[h][4 * i] = __float_as_uint(__uint_as_float(r[h][4 * i]) + v[i].x);
+                r[h][4 * i + 1] = __float_as_uint(__uint_as_float(r[h][4 * i + 1]) + v[i].y);
+                r[h][4 * i + 2] = __float_as_uint(__uint_as_float(r[h][4 * i + 2]) + v[i].z);
+                r[h][4 * i + 3] = __float_as_uint(__uint_as_float(r[h][4 * i + 3]) + v[i].w);
+              }
+            }
+          }
+          if (kDual) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              r[0][i] = __float_as_uint(silu_mul(__uint_as_float(r[0][i]), __uint_as_float(r[kHalves - 1][i])));
+          }
+          store_half_row32(crow + o * 32, r[0]);
+        }
+        if (!fix_ok) set_status(p.status, kStatusTimeoutPeer);
+        if (threadIdx.x == 64 && nc > 0) TRACE_STAMP(17);
+        // tcgen05.wait::ld completed the reads; a relaxed arrive suffices
+        // (see the scale writers).
+        tc_fence_before();
+        mbar_arrive_cluster_relaxed(acc_empty0);
       }
-      tc_fence_before();
-      mbar_arrive_cluster(acc_empty0);
       acc_phase ^= 1;
     }
   }
 
 #ifdef NVFP4_TRACE
+  if (threadIdx.x == 64) TRACE_STAMP(11);
   if (warp == 1) TRACE_TOTAL(2);
   if (warp == 6) TRACE_TOTAL(5);
   if (warp == 2) TRACE_TOTAL(7);
@@ -990,6 +1194,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     __syncwarp();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
+  if (threadIdx.x == 0) TRACE_STAMP(12);
+  TRACE_CLOCK(15);
 }
 
 // ------------------------------------------------------------------ host side
@@ -1104,6 +1310,11 @@ static bool make_operand_map(CUtensorMap* map, const void* base, int K2, int row
   return make_tma_3d_u8(map, base, K2, rows, L, K2, lstride, kBKBytes, box_rows);
 }
 
+static int env_int(const char* name) {
+  const char* e = getenv(name);
+  return e ? atoi(e) : 0;
+}
+
 template <int BN, bool kDual>
 static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {
   using Cfg = GemmConfig<BN, kDual>;
@@ -1147,27 +1358,24 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
   p.splits = g.splits > 1 ? g.splits : 1;
   p.num_items = p.num_tiles * p.splits;
   p.streamk = (!kDual && p.splits == 1 && g.streamk && g.workspace) ? 1 : 0;
-  p.units = static_cast<int64_t>(p.num_tiles) * (g.K / kBK);
   p.sk_flag = static_cast<int*>(g.workspace);
   p.sk_partial = p.streamk ? reinterpret_cast<float*>(static_cast<uint8_t*>(g.workspace) + kStreamKFlagBytes) : nullptr;
   // Test hook for the bounded-wait path (tests/test_failure_detection.py):
   // the kernel then reports a pipeline timeout instead of hanging.
   const char* fi = getenv("NVFP4_FAULT_INJECT");
   p.inject = (fi && fi[0] == '1' && p.splits == 1) ? 1 : 0;
+  p.prefetch = env_int("NVFP4_PREFETCH");
   // Without split: a persistent grid.  With split K: one CTA per (tile,
   // split), the splits of a tile in one cluster.
   const int grid = p.splits == 1 ? (p.num_items < num_sms ? p.num_items : num_sms) : p.num_items;
+  p.dp_tiles = g.streamk_pure ? 0 : (p.num_tiles / grid) * grid;
+  p.units = static_cast<int64_t>(p.num_tiles - p.dp_tiles) * (g.K / kBK);
   if (p.streamk && grid * (kBM * BN * 4) + kStreamKFlagBytes > static_cast<int64_t>(g.workspace_bytes)) {
     *why = "stream-K workspace too small";
     return cudaErrorInvalidValue;
   }
   return launch_pdl(gemm_kernel<BN, kDual>, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, stream, p.splits, ta, tb,
                     tb2, p);
-}
-
-static int env_int(const char* name) {
-  const char* e = getenv(name);
-  return e ? atoi(e) : 0;
 }
 
 // Tile width and K splits for a problem.  Problems with fewer tiles than SMs
@@ -1236,37 +1444,63 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms) {
   pl.splits = splits < 1 ? 1 : splits;
   pl.workspace_bytes = 0;
   pl.streamk = 0;
+  pl.streamk_pure = 0;
   pl.pair = 0;
-  // Stream-K when whole tiles leave the last wave part-empty: e.g. 224 tiles
-  // on 148 SMs run as two tile-waves (76 SMs busy in the second) against
-  // ceil(224 * KT / 148) K tiles per SM in equal ranges.  Worth it when the
-  // busiest SM's K tiles drop by more than 10%.
   // 2-CTA pairs (256x256 tiles) whenever the shape allows: per K tile each
   // SM moves 32 KB through shared memory for TMA writes and 32 KB for MMA
   // reads instead of 48 + 48 KB with 128x256 tiles (measured +17% on
   // 1024x7168x16384, +27% on 16384^3).  NVFP4_PAIR=0 keeps 1-CTA tiles.
+  // The dual GEMM runs on pairs (256 x (128 B1 + 128 B2) tiles, whole tiles)
+  // when M % 256 == 0 and the pair tiles fill at least ~2/3 of the pairs
+  // (measured: 512x4096x7168 18.8 us against 20.4 on 1-CTA tiles with K
+  // split in clusters; with half the pairs busy, 256x4096x7168, the 1-CTA
+  // split is faster).  Splitting K across pairs (stream-K, NVFP4_STREAMK=2)
+  // costs a trip of fp32 partial tiles through L2, measured slower.
   const char* pe = getenv("NVFP4_PAIR");
-  pl.pair = (!dual && pl.bn == 256 && pl.splits == 1 && M % 256 == 0 && !(pe && pe[0] == '0')) ? 1 : 0;
-  const int forced_sk = env_int("NVFP4_STREAMK");  // 1 force on, -1 force off
-  if (!dual && !pl.pair && pl.splits == 1 && tiles > num_sms && forced_sk >= 0) {
-    const int64_t classic = static_cast<int64_t>((tiles + num_sms - 1) / num_sms) * KT;
-    const int64_t units = static_cast<int64_t>(tiles) * KT;
-    const int64_t sk = (units + num_sms - 1) / num_sms + 2;  // +2: partial write / read
-    if (forced_sk == 1 || sk * 10 < classic * 9) {
+  const bool pair_on = pe && pe[0] == '1', pair_off = pe && pe[0] == '0';
+  pl.pair = (!dual && pl.bn == 256 && pl.splits == 1 && M % 256 == 0 && !pair_off) ? 1 : 0;
+  if (dual && M % 256 == 0 && !pair_off && (pair_on || 3 * ((M / 256) * (N / 128) * L) >= 2 * (num_sms / 2))) {
+    pl.pair = 1;
+    pl.splits = 1;
+  }
+  // Stream-K (hybrid) when whole tiles leave the last wave part-empty: e.g.
+  // 112 pair tiles on 74 pairs run as two tile-waves, 38 pairs busy in the
+  // second; instead every worker takes one whole tile and then ~0.51 of a
+  // tile's K range of the 38 left over.  Used when the busiest worker's K
+  // tiles drop by more than 10%.  NVFP4_STREAMK: 1 force on, 2 force the
+  // pure form (no whole-tile waves), -1 force off.
+  const int forced_sk = env_int("NVFP4_STREAMK");
+  const int wtiles = pl.pair ? (M / 256) * (N / (dual ? 128 : 256)) * L : tiles;
+  const int workers = pl.pair ? num_sms / 2 : num_sms;
+  if (pl.pair && wtiles < workers && forced_sk == 2) {
+    // Fewer pair tiles than pairs: pure stream-K spreads the K tiles over all
+    // pairs (a tile's K range then spans about workers / tiles pairs).
+    pl.streamk = 1;
+    pl.streamk_pure = 1;
+    pl.workspace_bytes = kStreamKFlagBytes + static_cast<size_t>(2 * workers) * 128 * 256 * 4;
+  } else if ((pl.pair || (!dual && pl.splits == 1)) && forced_sk >= 0 && wtiles > workers) {
+    const int64_t classic = static_cast<int64_t>((wtiles + workers - 1) / workers) * KT;
+    const int rest = wtiles % workers;
+    const int64_t hybrid =
+        static_cast<int64_t>(wtiles / workers) * KT + (static_cast<int64_t>(rest) * KT + workers - 1) / workers + 2;
+    if (forced_sk >= 1 || (rest != 0 && hybrid * 10 < classic * 9)) {
       pl.streamk = 1;
-      pl.workspace_bytes = kStreamKFlagBytes + static_cast<size_t>(num_sms) * 128 * pl.bn * 4;
+      pl.streamk_pure = forced_sk == 2 ? 1 : 0;
+      pl.workspace_bytes =
+          kStreamKFlagBytes + static_cast<size_t>(pl.pair ? 2 * workers : workers) * 128 * 256 * 4;
     }
   }
   return pl;
 }
 
+template <bool kDual>
 static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {
   static bool attr_done[64] = {false};
   static int max_pairs[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<kDual>, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::kSmem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
@@ -1280,7 +1514,7 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel, &cfg) != cudaSuccess || n < 1) {
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<kDual>, &cfg) != cudaSuccess || n < 1) {
       cudaGetLastError();
       n = num_sms / 2;
     }
@@ -1288,17 +1522,20 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
     attr_done[dev] = true;
   }
   const uint64_t K2 = g.K / 2;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tb2;
   if (!make_operand_map(&ta, g.a, K2, g.M, g.L, g.a_lstride, 128) ||
-      !make_operand_map(&tb, g.b, K2, g.N, g.L, g.b_lstride, 128)) {
+      !make_operand_map(&tb, g.b, K2, g.N, g.L, g.b_lstride, 128) ||
+      (kDual && !make_operand_map(&tb2, g.b2, K2, g.N, g.L, g.b2_lstride, 128))) {
     *why = "cuTensorMapEncodeTiled failed";
     return cudaErrorInvalidValue;
   }
   GemmParams p{};
   p.sfa = static_cast<const uint8_t*>(g.sfa);
   p.sfb = static_cast<const uint8_t*>(g.sfb);
+  p.sfb2 = static_cast<const uint8_t*>(g.sfb2);
   p.sfa_lstride = g.sfa_lstride;
   p.sfb_lstride = g.sfb_lstride;
+  p.sfb2_lstride = g.sfb2_lstride;
   p.c = static_cast<__half*>(g.c);
   p.M = g.M;
   p.N = g.N;
@@ -1307,25 +1544,41 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
   p.ldc = g.ldc;
   p.c_lstride = g.c_lstride;
   p.tiles_m = g.M / 256;
-  p.tiles_n = g.N / 256;
+  p.tiles_n = g.N / (kDual ? 128 : 256);
   p.num_tiles = p.tiles_m * p.tiles_n * g.L;
   p.group_m = p.tiles_m < 8 ? p.tiles_m : 8;
   p.status = g.status;
   p.splits = 1;
   p.num_items = p.num_tiles;
+  p.streamk = (g.streamk && g.workspace) ? 1 : 0;
+  // Whole tiles: at most one pair per tile.  Stream-K: every co-resident
+  // pair (at most one per K tile).
   int pairs = max_pairs[dev < 64 ? dev : 0];
-  if (pairs > p.num_tiles) pairs = p.num_tiles;
+  // (Stream-K: at most 8 pairs per tile, so a tile's K range spans at most
+  // ~10 pairs, within the finaliser's pair::kMaxContrib.)
+  const int64_t kts = g.K / kBK;
+  const int64_t work = p.streamk ? static_cast<int64_t>(p.num_tiles) * (kts < 8 ? kts : 8) : p.num_tiles;
+  if (pairs > work) pairs = static_cast<int>(work);
   if (pairs < 1) pairs = 1;
-  return launch_pdl(gemm_pair_kernel, dim3(2 * pairs), dim3(kPairThreads), pair::kSmem, stream, 2, ta, tb, p);
+  p.dp_tiles = g.streamk_pure ? 0 : (p.num_tiles / pairs) * pairs;
+  p.units = static_cast<int64_t>(p.num_tiles - p.dp_tiles) * (g.K / kBK);
+  p.sk_flag = static_cast<int*>(g.workspace);
+  p.sk_partial = p.streamk ? reinterpret_cast<float*>(static_cast<uint8_t*>(g.workspace) + kStreamKFlagBytes) : nullptr;
+  if (p.streamk && static_cast<size_t>(2 * pairs) * 128 * 256 * 4 + kStreamKFlagBytes > g.workspace_bytes) {
+    *why = "stream-K workspace too small";
+    return cudaErrorInvalidValue;
+  }
+  return launch_pdl(gemm_pair_kernel<kDual>, dim3(2 * pairs), dim3(kPairThreads), pair::kSmem, stream, 2, ta, tb, kDual ? tb2 : tb, p);
 }
 
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {
-  if (g.pair) return launch_pair(g, num_sms, stream, why);
+  if (g.pair) return launch_pair<false>(g, num_sms, stream, why);
   if (g.bn == 256) return launch_impl<256, false>(g, num_sms, stream, why);
   return launch_impl<128, false>(g, num_sms, stream, why);
 }
 
 cudaError_t launch_dual_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {
+  if (g.pair) return launch_pair<true>(g, num_sms, stream, why);
   return launch_impl<128, true>(g, num_sms, stream, why);
 }
 
@@ -1334,7 +1587,7 @@ cudaError_t launch_dual_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream
 #ifdef NVFP4_TRACE
 extern "C" __attribute__((visibility("default"))) int nvfp4_dbg_gemm_trace(unsigned long long* host) {
   if (cudaMemcpyFromSymbol(host, nvfp4::g_gemm_trace, sizeof(nvfp4::g_gemm_trace)) != cudaSuccess) return 1;
-  static unsigned long long zero[1024 * 8];
+  static unsigned long long zero[1024 * 32];
   return cudaMemcpyToSymbol(nvfp4::g_gemm_trace, zero, sizeof(zero)) != cudaSuccess;
 }
 #endif

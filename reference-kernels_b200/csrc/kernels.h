@@ -82,7 +82,7 @@ struct GemmArgs {
   int64_t sfa_lstride, sfb_lstride, sfb2_lstride;  // bytes
   int64_t ldc, c_lstride;                          // elements
   int* status;                                     // device status word (bounded-wait timeouts)
-  int bn, splits, streamk, pair;                   // from gemm_plan
+  int bn, splits, streamk, streamk_pure, pair;     // from gemm_plan
   void* workspace;                                 // stream-K partials + flags (zeroed once; left zeroed)
   size_t workspace_bytes;
 };
@@ -90,6 +90,7 @@ struct GemmPlan {
   int bn;      // N tile: 128 or 256
   int splits;  // K splits per tile
   int streamk;  // 1: stream-K ranges over (tile, K tile) units (plain GEMM, tiles > SMs)
+  int streamk_pure;  // 1: no whole-tile waves before the stream-K ranges (tests / comparison)
   int pair;     // 1: 2-CTA kernel, 256x256 tiles (plain GEMM, M % 256 == 0, N % 256 == 0, no split)
   size_t workspace_bytes;  // stream-K partial slots + flags; 0 otherwise (split K reduces on chip)
 };

@@ -161,21 +161,27 @@ def test_pair_gemm_matches_single_cta_and_oracle(m, n, k, l, monkeypatch):
         assert_match(pair1, oracle_ref("gemm", data), f"pair vs oracle {m}x{n}x{k}x{l}")
 
 
+@pytest.mark.parametrize("form", ["hybrid", "pure"])
+@pytest.mark.parametrize("kernel", ["single", "pair"])
 @pytest.mark.parametrize("m,n,k,l", [
     (1664, 3072, 512, 1),    # 156 tiles of 128x256, ~2.1 K tiles per CTA: tiles cut three ways
     (1280, 2176, 1024, 1),   # N % 256 != 0: 128x128 tiles, 170 of them
-    (1024, 7168, 2048, 1),   # benchmark config's M, N (224 tiles), short K
+    (1024, 7168, 2048, 1),   # benchmark config's M, N (224 tiles / 112 pair tiles), short K
     (768, 3328, 1280, 2),    # L = 2: ranges cross batch boundaries
+    (2560, 4096, 512, 1),    # 160 pair tiles, ~4.3 K tiles per pair: pair tiles cut three ways
 ])
-def test_stream_k_gemm(m, n, k, l, monkeypatch):
-    """Stream-K GEMM (equal (tile, K tile) ranges per CTA, partial tiles
-    combined through the workspace) against the oracle / _scaled_mm, the
-    classic tile-per-CTA path, and itself (bit-identical on repeat)."""
+def test_stream_k_gemm(m, n, k, l, kernel, form, monkeypatch):
+    """Stream-K GEMM (equal (tile, K tile) ranges per CTA or CTA pair, after
+    whole-tile waves in the hybrid form; partial tiles combined through the
+    workspace) against the oracle / _scaled_mm, the classic tile-per-worker
+    path, and itself (bit-identical on repeat)."""
+    if kernel == "pair" and (m % 256 or n % 256):
+        pytest.skip("2-CTA tiles need M % 256 == 0 and N % 256 == 0")
     data = inputs.baseline_input("gemm", m, k, l, 33, n=n)
-    monkeypatch.setenv("NVFP4_PAIR", "0")  # stream-K runs on the 1-CTA kernel
+    monkeypatch.setenv("NVFP4_PAIR", "1" if kernel == "pair" else "0")
     monkeypatch.setenv("NVFP4_STREAMK", "-1")
     classic = run("gemm", data).clone()
-    monkeypatch.setenv("NVFP4_STREAMK", "1")
+    monkeypatch.setenv("NVFP4_STREAMK", "1" if form == "hybrid" else "2")
     sk1 = run("gemm", data).clone()
     sk2 = run("gemm", data).clone()
     assert torch.equal(sk1, sk2)
@@ -184,3 +190,35 @@ def test_stream_k_gemm(m, n, k, l, monkeypatch):
         assert_match(sk1, oracle_ref("gemm", data), f"stream-K vs oracle {m}x{n}x{k}x{l}")
     else:
         assert_match(sk1, scaled_mm_ref("gemm", data), f"stream-K vs _scaled_mm {m}x{n}x{k}x{l}")
+
+
+@pytest.mark.parametrize("kernel", ["single", "pair"])
+@pytest.mark.parametrize("m,n,k", [(256, 512, 1024), (512, 384, 2048), (384, 512, 1024), (256, 4096, 7168)])
+def test_dual_single_and_pair_kernels(m, n, k, kernel, monkeypatch):
+    """Dual GEMM on the 1-CTA kernel (128 x (B1|B2) tiles, K split in
+    clusters) and on the 2-CTA kernel (256 x (B1|B2) tiles, K split by
+    stream-K ranges) against the oracle / _scaled_mm, repeated bit-identically."""
+    if kernel == "pair" and m % 256:
+        pytest.skip("2-CTA tiles need M % 256 == 0")
+    monkeypatch.setenv("NVFP4_PAIR", "1" if kernel == "pair" else "0")
+    data = inputs.baseline_input("dual", m, k, 1, 44, n=n)
+    out1 = run("dual", data).clone()
+    out2 = run("dual", data).clone()
+    assert torch.equal(out1, out2)
+    if m * n * k <= 512 * 512 * 2048:
+        assert_match(out1, oracle_ref("dual", data), f"dual {kernel} {m}x{n}x{k} vs oracle")
+    else:
+        assert_match(out1, scaled_mm_ref("dual", data), f"dual {kernel} {m}x{n}x{k} vs _scaled_mm")
+
+
+@pytest.mark.parametrize("problem,m,n,k", [("dual", 256, 128, 7168), ("dual", 256, 256, 2048), ("gemm", 256, 256, 7168)])
+def test_pair_stream_k_many_contributors(problem, m, n, k, monkeypatch):
+    """One or two tiles spread over many pairs (pure stream-K, up to ~10
+    pairs per tile): the finaliser combines many partial slots."""
+    monkeypatch.setenv("NVFP4_PAIR", "1")
+    monkeypatch.setenv("NVFP4_STREAMK", "2")
+    data = inputs.baseline_input(problem, m, k, 1, 55, n=n)
+    out1 = run(problem, data).clone()
+    out2 = run(problem, data).clone()
+    assert torch.equal(out1, out2)
+    assert_match(out1, oracle_ref(problem, data), f"{problem} {m}x{n}x{k} many contributors vs oracle")
