@@ -48,7 +48,7 @@ CONFIGS = {
 # committed ncu summaries (profiles/<name>.txt) of each workload's kernel
 PROFILE_NAMES = {
     "gemv": "gemv_tc_kernel_M7168_K16384_L4",
-    "gemm": "gemm_kernel_M1024_N7168_K16384",
+    "gemm": "gemm_pair_kernel_M1024_N7168_K16384",
     "dual": "dual_gemm_kernel_M256_N4096_K7168",
 }
 

@@ -1102,7 +1102,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             abort_flag = 1;
             break;
           }
-          if (threadIdx.x == 64) TRACE_STAMP(16);
         }
         // The contributors' partials are streamed into shared memory (free
         // now: this is the CTA's last segment and its MMAs are complete) by
@@ -1138,9 +1137,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             tmem_wait_ld();
             for (int j = 0; j < nc; ++j, ++q) {
               fix_ok &= mbar_wait(&fix_full[q % kFixBufs], (q / kFixBufs) & 1);
-#ifdef NVFP4_TRACE
-              if (threadIdx.x == 64 && q < 12) TRACE_STAMP(18 + q);
-#endif
               const float4* buf = reinterpret_cast<const float4*>(smem + (q % kFixBufs) * kFixChunk) + rloc;
               float4 v[8];
 #pragma unroll
@@ -1168,7 +1164,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           store_half_row32(crow + o * 32, r[0]);
         }
         if (!fix_ok) set_status(p.status, kStatusTimeoutPeer);
-        if (threadIdx.x == 64 && nc > 0) TRACE_STAMP(17);
         // tcgen05.wait::ld completed the reads; a relaxed arrive suffices
         // (see the scale writers).
         tc_fence_before();
