@@ -1061,7 +1061,28 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const int row = mb * 256 + static_cast<int>(rank) * 128 + rloc;
       __half* crow = p.c + l * p.c_lstride + static_cast<int64_t>(row) * p.ldc + static_cast<int64_t>(nb) * (kDual ? 128 : 256);
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-      if (p.streamk && k0 > 0) {
+      if (!p.streamk) {
+        // Whole tile (the common case), kept compact and ahead of the
+        // stream-K paths.
+#pragma unroll 1
+        for (int o = 0; o < (kDual ? 4 : 8); ++o) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tacc + o * 32, r);
+          if (kDual) {
+            uint32_t r2[32];
+            tmem_ld_32x32b_x32(tacc + o * 32 + 128, r2);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              r[i] = __float_as_uint(silu_mul(__uint_as_float(r[i]), __uint_as_float(r2[i])));
+          } else {
+            tmem_wait_ld();
+          }
+          store_half_row32(crow + o * 32, r);
+        }
+        tc_fence_before();
+        mbar_arrive_cluster_relaxed(acc_empty0);
+      } else if (k0 > 0) {
         // Contributor: this CTA's 128 rows of the partial tile to its slot
         // ([column group][float4 index][row][4] floats), then its flag.
         float4* dst = reinterpret_cast<float4*>(p.sk_partial) + static_cast<int64_t>(my_slot) * (128 * 256 / 4) + rloc;
