@@ -107,7 +107,8 @@ int nvfp4_gemv_noalloc(const void* a, const void* b, const void* sfa_blk, const 
  *   sfa_blk : blocked scales of A   sfa_lstride (bytes, = M*K/16 for the reference tensors)
  *   sfb_blk : blocked scales of B   sfb_lstride (bytes)
  *   c       : fp16 [L][M][ldc]      ldc, c_lstride (elements)
- * Requires M % 128 == 0, N % 128 == 0, K % 256 == 0 (task.yml of the problem),
+ * Requires M % 128 == 0, N % 128 == 0, K % 64 == 0 (the blocked scale layout;
+ * K % 256 != 0 runs a partial last K tile),
  * 16-byte aligned bases and batch strides.  An N-shard of a larger problem is
  * passed as b + n0*K/2, sfb_blk + (n0/128)*K*8, c + n0 with ldc = full N. */
 int nvfp4_gemm(const void* a, const void* b, const void* sfa_blk, const void* sfb_blk, void* c, int M, int N, int K,

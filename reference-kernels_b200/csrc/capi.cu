@@ -182,7 +182,7 @@ static int check_gemm_common(const char* name, const void* a, const void* b, con
   if (M <= 0 || N <= 0 || K <= 0 || L <= 0) return fail(NVFP4_ERR_SHAPE, "%s: sizes must be positive", name);
   if (M % 128 || N % 128)
     return fail(NVFP4_ERR_SHAPE, "%s: M=%d and N=%d must be multiples of 128", name, M, N);
-  if (K % 256) return fail(NVFP4_ERR_SHAPE, "%s: K=%d must be a multiple of 256", name, K);
+  if (K % 64) return fail(NVFP4_ERR_SHAPE, "%s: K=%d must be a multiple of 64", name, K);
   if (ldc < N) return fail(NVFP4_ERR_SHAPE, "%s: ldc=%lld < N=%d", name, (long long)ldc, N);
   if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sfa, 16) || !aligned(sfb, 16) || !aligned(c, 16) ||
       (a_lstride % 16) || (b_lstride % 16) || (sfa_lstride % 16) || (sfb_lstride % 16) || (ldc % 8) ||

@@ -109,7 +109,6 @@ struct GemmConfig {
   static constexpr int kTmemCols = 512;
   static_assert(kAccBufs * kAccCols + kStages * kSfCols <= kTmemCols, "TMEM budget");
   static constexpr int kTxBytes = kStageBytes;                 // full[]: A and B tiles
-  static constexpr int kSfTxBytes = kSfOps * kSfStageBytes;     // sf_full[]: the stage's scale runs
   static constexpr int kSmemBytes =
       1024 /*align slack*/ + kStages * (kStageBytes + kSfOps * kSfStageBytes) + 256 /*barriers*/;
 };
@@ -148,6 +147,15 @@ struct GemmParams {
   int* sk_flag;       // gridDim.x flags, 0 between launches
   int* status;
 };
+
+// MMA K steps (of 64) in K tile kt: 4, or fewer in a partial last tile.
+__device__ __forceinline__ int ksteps(int K, int kt) {
+  const int r = (K - kt * 256) / 64;
+  return r < 4 ? r : 4;
+}
+
+// Bytes of one 128-row block's scale run in K tile kt (2 KB, less in a partial tile).
+__device__ __forceinline__ uint32_t sf_run_bytes(int K, int kt) { return static_cast<uint32_t>(ksteps(K, kt)) * 512u; }
 
 // K-tile range [k0, k1) of split s.
 __device__ __forceinline__ void split_range(int KT, int splits, int s, int& k0, int& k1) {
@@ -320,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KT = p.K / kBK;
+  const int KT = (p.K + kBK - 1) / kBK;  // the last K tile may be partial (K % 64 == 0)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -379,17 +387,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sf = sfbuf + stage * Cfg::kSfOps * kSfStageBytes;
           // Scales first, on their own barrier: the writers can put them in
           // TMEM while the larger A/B tiles are still arriving.
-          mbar_arrive_expect_tx(&sf_full[stage], Cfg::kSfTxBytes);
-          bulk_load(sf, sfa_src + kt * kSfStageBytes, kSfStageBytes, &sf_full[stage], pol_a);
+          const uint32_t sfb_bytes = sf_run_bytes(p.K, kt);
+          mbar_arrive_expect_tx(&sf_full[stage], Cfg::kSfOps * sfb_bytes);
+          bulk_load(sf, sfa_src + kt * kSfStageBytes, sfb_bytes, &sf_full[stage], pol_a);
 #pragma unroll
           for (int j = 0; j < BN / 128; ++j)
             bulk_load(sf + (1 + j) * kSfStageBytes, sfb_src + static_cast<int64_t>(j) * p.K * 8 + kt * kSfStageBytes,
-                      kSfStageBytes, &sf_full[stage], pol_b);
+                      sfb_bytes, &sf_full[stage], pol_b);
           if (kDual) {
 #pragma unroll
             for (int j = 0; j < BN / 128; ++j)
               bulk_load(sf + (1 + BN / 128 + j) * kSfStageBytes,
-                        sfb2_src + static_cast<int64_t>(j) * p.K * 8 + kt * kSfStageBytes, kSfStageBytes,
+                        sfb2_src + static_cast<int64_t>(j) * p.K * 8 + kt * kSfStageBytes, sfb_bytes,
                         &sf_full[stage], pol_b);
           }
           mbar_arrive_expect_tx(&full[stage], Cfg::kTxBytes);
@@ -443,8 +452,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           TRACE_ISSUE_BEGIN;
           const uint32_t st = smem_u32(tiles + stage * Cfg::kStageBytes);
           const uint32_t sfc = tmem_base + sf_col0 + stage * Cfg::kSfCols;
+          const int nkk = ksteps(p.K, kt);
 #pragma unroll
           for (int kk = 0; kk < kBK / kMmaK; ++kk) {
+            if (kk >= nkk) break;
             const uint64_t adesc = desc_kmajor_sw128(st + kk * (kMmaK / 2));
             const uint64_t bdesc = desc_kmajor_sw128(st + Cfg::kABytes + kk * (kMmaK / 2));
             const uint32_t accum = (kt != k0 || kk != 0) ? 1u : 0u;
@@ -776,7 +787,6 @@ constexpr int kSfa = kSfStageBytes;      // 2 KB
 constexpr int kSfb = 2 * kSfStageBytes;  // 4 KB: both 128-row blocks of the tile's N
 constexpr int kStage = kA + kB + kSfa + kSfb;
 constexpr int kTx = 2 * (kA + kB);  // the leader's full barrier counts both CTAs' A and B bytes
-constexpr int kSfTx = kSfa + kSfb;  // each CTA's own sf_full barrier: its scale runs
 constexpr int kAccCols = 256;
 constexpr int kSfCols = 48;
 constexpr int kTmemCols = 512;
@@ -869,7 +879,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KT = p.K / kBK;
+  const int KT = (p.K + kBK - 1) / kBK;  // the last K tile may be partial (K % 64 == 0)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair_id = blockIdx.x >> 1, npairs = gridDim.x >> 1;
@@ -936,11 +946,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           tma_load_3d_pair(st + kA, bmap, bar0, kt * kBKBytes, brow, l, pol_b);
           // Scales into this CTA's own shared memory, on its own barrier: SFA
           // of its 128 rows, SFB of both 128-row blocks of the tile's N.
-          mbar_arrive_expect_tx(&sf_full[stage], kSfTx);
-          bulk_load(st + kA + kB, sfa_src + kt * kSfStageBytes, kSfStageBytes, &sf_full[stage], pol_a);
-          bulk_load(st + kA + kB + kSfa, sfb_src0 + kt * kSfStageBytes, kSfStageBytes, &sf_full[stage], pol_b);
-          bulk_load(st + kA + kB + kSfa + kSfStageBytes, sfb_src1 + kt * kSfStageBytes, kSfStageBytes,
-                    &sf_full[stage], pol_b);
+          const uint32_t sf_bytes = sf_run_bytes(p.K, kt);
+          mbar_arrive_expect_tx(&sf_full[stage], 3 * sf_bytes);
+          bulk_load(st + kA + kB, sfa_src + kt * kSfStageBytes, sf_bytes, &sf_full[stage], pol_a);
+          bulk_load(st + kA + kB + kSfa, sfb_src0 + kt * kSfStageBytes, sf_bytes, &sf_full[stage], pol_b);
+          bulk_load(st + kA + kB + kSfa + kSfStageBytes, sfb_src1 + kt * kSfStageBytes, sf_bytes, &sf_full[stage],
+                    pol_b);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -974,9 +985,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           tc_fence_after();
           const uint32_t st = smem_u32(smem + stage * kStage);
           const uint32_t sfc = tmem_base + sf_col0 + stage * kSfCols;
+          const int nkk = ksteps(p.K, kt);
 #pragma unroll
           for (int kk = 0; kk < kBK / kMmaK; ++kk)
-            mma_nvf4_pair(tmem_base, desc_kmajor_sw128(st + kk * (kMmaK / 2)),
+            if (kk < nkk)
+              mma_nvf4_pair(tmem_base, desc_kmajor_sw128(st + kk * (kMmaK / 2)),
                           desc_kmajor_sw128(st + kA + kk * (kMmaK / 2)), idesc, sfc + 4 * kk, sfc + 16 + 8 * kk,
                           (kt != k0 || kk != 0) ? 1u : 0u);
           tc_commit_pair_mc(&empty[stage], 0x3);
@@ -1385,7 +1398,7 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
   // split), the splits of a tile in one cluster.
   const int grid = p.splits == 1 ? (p.num_items < num_sms ? p.num_items : num_sms) : p.num_items;
   p.dp_tiles = g.streamk_pure ? 0 : (p.num_tiles / grid) * grid;
-  p.units = static_cast<int64_t>(p.num_tiles - p.dp_tiles) * (g.K / kBK);
+  p.units = static_cast<int64_t>(p.num_tiles - p.dp_tiles) * ((g.K + kBK - 1) / kBK);
   if (p.streamk && grid * (kBM * BN * 4) + kStreamKFlagBytes > static_cast<int64_t>(g.workspace_bytes)) {
     *why = "stream-K workspace too small";
     return cudaErrorInvalidValue;
@@ -1438,7 +1451,7 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms) {
   const int forced_bn = env_int("NVFP4_GEMM_BN");
   pl.bn = (!dual && N % 256 == 0 && forced_bn != 128) ? 256 : 128;
   const int tiles = (M / 128) * (N / pl.bn) * L;
-  const int KT = K / 256;
+  const int KT = (K + 255) / 256;
   const int ngroups = pl.bn / 32;  // a split owns at least one 32-column group of the tile
   int splits = 1;
   if (tiles < num_sms) splits = num_sms / tiles;
@@ -1572,12 +1585,12 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
   int pairs = max_pairs[dev < 64 ? dev : 0];
   // (Stream-K: at most 8 pairs per tile, so a tile's K range spans at most
   // ~10 pairs, within the finaliser's pair::kMaxContrib.)
-  const int64_t kts = g.K / kBK;
+  const int64_t kts = (g.K + kBK - 1) / kBK;
   const int64_t work = p.streamk ? static_cast<int64_t>(p.num_tiles) * (kts < 8 ? kts : 8) : p.num_tiles;
   if (pairs > work) pairs = static_cast<int>(work);
   if (pairs < 1) pairs = 1;
   p.dp_tiles = g.streamk_pure ? 0 : (p.num_tiles / pairs) * pairs;
-  p.units = static_cast<int64_t>(p.num_tiles - p.dp_tiles) * (g.K / kBK);
+  p.units = static_cast<int64_t>(p.num_tiles - p.dp_tiles) * ((g.K + kBK - 1) / kBK);
   p.sk_flag = static_cast<int*>(g.workspace);
   p.sk_partial = p.streamk ? reinterpret_cast<float*>(static_cast<uint8_t*>(g.workspace) + kStreamKFlagBytes) : nullptr;
   if (p.streamk && static_cast<size_t>(2 * pairs) * 128 * 256 * 4 + kStreamKFlagBytes > g.workspace_bytes) {

@@ -222,3 +222,25 @@ def test_pair_stream_k_many_contributors(problem, m, n, k, monkeypatch):
     out2 = run(problem, data).clone()
     assert torch.equal(out1, out2)
     assert_match(out1, oracle_ref(problem, data), f"{problem} {m}x{n}x{k} many contributors vs oracle")
+
+
+@pytest.mark.parametrize("kernel", ["single", "pair", "streamk"])
+@pytest.mark.parametrize("problem,m,n,k,l", [
+    ("gemm", 256, 256, 64, 1), ("gemm", 256, 512, 192, 2), ("gemm", 512, 512, 320, 1), ("gemm", 256, 768, 1856, 1),
+    ("gemm", 2048, 2560, 320, 1),  # 160 tiles: no K split, so the 2-CTA kernel runs under "pair"
+    ("dual", 256, 256, 448, 1), ("dual", 512, 384, 1344, 1),
+])
+def test_k_tail(problem, m, n, k, l, kernel, monkeypatch):
+    """K % 256 != 0 (K % 64 == 0): a partial last K tile issues only its
+    remaining 64-wide MMA steps and copies only their scale blocks; checked
+    on the 1-CTA kernel (with its K-split clusters), the pair kernel and
+    stream-K against the oracle."""
+    monkeypatch.setenv("NVFP4_PAIR", "1" if kernel == "pair" else "0")
+    if kernel == "streamk":
+        if problem == "dual":
+            pytest.skip("stream-K is a GEMM option")
+        monkeypatch.setenv("NVFP4_STREAMK", "2")
+        monkeypatch.setenv("NVFP4_PAIR", "0")
+    data = inputs.baseline_input(problem, m, k, l, 66, n=n)
+    out = run(problem, data).clone()
+    assert_match(out, oracle_ref(problem, data), f"{problem} {kernel} {m}x{n}x{k}x{l} K tail vs oracle")
