@@ -10,7 +10,9 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libnvfp4_b200.so")
+# NVFP4_B200_LIBRARY points at another build of the same C ABI (e.g. a variant
+# built for an A/B timing on one GPU); the default is the in-tree library.
+LIB_PATH = os.environ.get("NVFP4_B200_LIBRARY") or os.path.join(_HERE, "libnvfp4_b200.so")
 
 EXPORTS = (
     "nvfp4_last_error",
