@@ -834,10 +834,6 @@ __device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
-}
-
 __device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t addr) {
   asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
 }
@@ -1044,8 +1040,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       __syncwarp();
       // The stores are complete (tcgen05.wait::st) and ordered before this
       // signal (tcgen05.fence::before_thread_sync), so a relaxed arrive is
-      // enough; an arrive.release.cluster per stage measured ~1500 cycles
-      // and made this signal the pair kernel's bottleneck.
+      // enough; a release arrive at cluster scope per stage measured ~1500
+      // cycles and made this signal the pair kernel's bottleneck.
       if (lane == 0) mbar_arrive_cluster_relaxed(ready0 + stage * 8);
       if (++stage == S) {
         stage = 0;
