@@ -304,6 +304,37 @@ def run_suite(repeats=20):
     print(json.dumps({"suite": "reference_benchmarks", "geomean_time_over_sol": geo}), flush=True)
 
 
+def gather_check(problem, full_data, fn, world, rank, dist):
+    """Multi-GPU correctness evidence, outside the timed region: every rank's
+    slice of C (written by its shard's custom_kernel calls) is assembled with an
+    NCCL all-gather, and rank 0 compares it with the whole problem run on its
+    one GPU (rtol = atol = 1e-3, infinities equal — the reference's check; the
+    two runs tile and split K differently, so bit equality is not expected)."""
+    from nvfp4_b200 import shard
+    c = full_data[-1]
+    shape = tuple(c.shape)
+    axis = 0 if problem == "gemv" else 1
+    bounds = [shard.shard_bounds(shape[axis], world, r) for r in range(world)]
+    width = max(hi - lo for lo, hi in bounds)
+    mine = c[shard.output_slice(problem, shape, world, rank)]
+    pad_shape = list(shape)
+    pad_shape[axis] = width
+    send = torch.zeros(pad_shape, dtype=c.dtype, device=c.device)
+    send.narrow(axis, 0, mine.shape[axis]).copy_(mine)
+    recv = [torch.empty_like(send) for _ in range(world)]
+    dist.all_gather(recv, send)
+    if rank != 0:
+        return None
+    assembled = torch.cat([r.narrow(axis, 0, hi - lo) for r, (lo, hi) in zip(recv, bounds)], dim=axis)
+    fn(full_data)  # the whole problem on rank 0's GPU, into the same C buffer
+    if c.is_cuda:
+        torch.cuda.synchronize()
+    close = torch.isclose(assembled.float(), c.float(), rtol=1e-3, atol=1e-3, equal_nan=True)
+    bad = int((~close).sum())
+    return {"kind": "NCCL all_gather of the ranks' C slices vs the whole problem on rank 0's GPU",
+            "elements": int(close.numel()), "mismatches": bad, "ok": bad == 0}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -457,6 +488,8 @@ def main():
         dist.barrier()
     e_ms = float(e_ms)
 
+    check = gather_check(problem, one_full, fn, world, rank, dist) if dist else None
+
     # whole-job totals
     tot_bytes = bytes_step * world
     tot_flops = flops_step * world
@@ -504,6 +537,7 @@ def main():
                 "steps": e2e_steps, "ms_per_step": e_ms,
                 "path": "pinned host -> device copies of the tensors the kernel reads, custom_kernel, output -> host"},
         "gpu_launches": args.steps,
+        **({"check": check} if check else {}),
         "clocks": clocks,
     }
     if rank == 0 and world == 1:
