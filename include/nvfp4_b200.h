@@ -25,8 +25,9 @@
  *   C               : fp16, row m of slice l at c + l*c_lstride + m*ldc
  *
  * All calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy
- * default stream).  Only nvfp4_gemv (tensor-core path) uses a per-device
- * workspace, which the library allocates on the first call that needs it.  Every entry point returns 0 on
+ * default stream).  The tensor-core GEMV (always) and the GEMMs (only with
+ * stream-K switched on) use a per-device workspace, which the library
+ * allocates on the first call that needs it.  Every entry point returns 0 on
  * success or one of the NVFP4_ERR_* codes; nvfp4_last_error() then returns a
  * message (thread-local).  Nothing runs on the CPU: there is no fallback.
  */
@@ -51,7 +52,7 @@ enum {
 /* Message for the last non-zero return on this thread. */
 const char* nvfp4_last_error(void);
 
-/* ABI revision of this header (1). */
+/* ABI revision of this header (2: adds the packed-argument *_call forms). */
 int nvfp4_abi_version(void);
 
 /* Reads (and optionally clears) the current device's status word, which the
@@ -141,6 +142,39 @@ int nvfp4_scales_to_blocked(const void* plain, void* blk, int rows, int sk, int 
                             int64_t plain_lstride, int64_t blk_lstride, void* stream);
 int nvfp4_scales_from_blocked(const void* blk, void* plain, int rows, int sk, int L, int64_t plain_row_stride,
                               int64_t plain_lstride, int64_t blk_lstride, void* stream);
+
+/* Packed-argument forms of nvfp4_gemv / nvfp4_gemm / nvfp4_dual_gemm: the
+ * same arguments in one struct, the same behaviour and return codes.  For
+ * bindings whose per-argument conversion is costly (Python ctypes: ~2 us for
+ * the 16-argument scalar form, ~0.5 us for one struct pointer), the caller can
+ * keep one struct per input set and update only `stream` between calls. */
+typedef struct {
+  const void* a;
+  const void* b;
+  const void* sfa_blk;
+  const void* sfb_blk;
+  void* c;
+  int32_t M, K, L, reserved;
+  int64_t a_lstride, b_lstride, sfa_lstride, sfb_lstride, c_lstride;
+  void* stream;
+} nvfp4_gemv_args;
+
+typedef struct {
+  const void* a;
+  const void* b;        /* B (nvfp4_gemm_call) or B1 (nvfp4_dual_gemm_call) */
+  const void* b2;       /* B2; ignored by nvfp4_gemm_call */
+  const void* sfa_blk;
+  const void* sfb_blk;  /* blocked scales of B / B1 */
+  const void* sfb2_blk; /* blocked scales of B2; ignored by nvfp4_gemm_call */
+  void* c;
+  int32_t M, N, K, L;
+  int64_t a_lstride, b_lstride, sfa_lstride, sfb_lstride, ldc, c_lstride;
+  void* stream;
+} nvfp4_gemm_args;
+
+int nvfp4_gemv_call(const nvfp4_gemv_args* args);
+int nvfp4_gemm_call(const nvfp4_gemm_args* args);
+int nvfp4_dual_gemm_call(const nvfp4_gemm_args* args);
 
 #ifdef __cplusplus
 }

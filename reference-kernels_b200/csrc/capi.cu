@@ -94,13 +94,39 @@ static void* workspace_for(int kind, int dev, size_t bytes, cudaStream_t stream,
   return w.ptr;
 }
 
+extern "C" char** environ;
+
+namespace nvfp4 {
+EnvOptions read_env_options() {
+  EnvOptions o;
+  for (char** e = environ; e && *e; ++e) {
+    const char* v = *e;
+    if (strncmp(v, "NVFP4_", 6) != 0) continue;
+    v += 6;
+    auto key = [&](const char* k) -> const char* {  // value if v is "k=..."
+      const size_t n = strlen(k);
+      return (strncmp(v, k, n) == 0 && v[n] == '=') ? v + n + 1 : nullptr;
+    };
+    const char* x;
+    if ((x = key("GEMM_BN"))) o.gemm_bn = atoi(x);
+    else if ((x = key("SPLITS"))) o.splits = atoi(x);
+    else if ((x = key("PAIR"))) o.pair = (x[0] == '0') ? 0 : (x[0] == '1') ? 1 : -1;
+    else if ((x = key("STREAMK"))) o.streamk = atoi(x);
+    else if ((x = key("PREFETCH"))) o.prefetch = atoi(x);
+    else if ((x = key("FAULT_INJECT"))) o.fault_inject = (x[0] == '1');
+    else if ((x = key("GEMV_PATH"))) o.gemv_simt = (strcmp(x, "simt") == 0);
+  }
+  return o;
+}
+}  // namespace nvfp4
+
 static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 #define NVFP4_API extern "C" __attribute__((visibility("default")))
 
 NVFP4_API const char* nvfp4_last_error(void) { return g_err; }
 
-NVFP4_API int nvfp4_abi_version(void) { return 1; }
+NVFP4_API int nvfp4_abi_version(void) { return 2; }
 
 NVFP4_API int nvfp4_device_status(int clear) {
   int dev = 0;
@@ -127,8 +153,8 @@ NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa_blk, cons
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4_ERR_DEVICE, "nvfp4_gemv: no CUDA device");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const char* path = getenv("NVFP4_GEMV_PATH");
-  const bool simt = (K % 256 != 0) || (path && strcmp(path, "simt") == 0) ||
+  const EnvOptions opt = read_env_options();
+  const bool simt = (K % 256 != 0) || opt.gemv_simt ||
                     gemv_tc_workspace_bytes(M, K, L, num_sms_of(dev)) == 0;
   if (!simt) {
     GemvTcArgs g{};
@@ -240,7 +266,10 @@ NVFP4_API int nvfp4_gemm(const void* a, const void* b, const void* sfa_blk, cons
   g.ldc = ldc;
   g.c_lstride = c_lstride;
   g.status = status_ptr(dev);
-  const GemmPlan pl = gemm_plan(M, N, K, L, false, num_sms_of(dev));
+  const EnvOptions opt = read_env_options();
+  const GemmPlan pl = gemm_plan(M, N, K, L, false, num_sms_of(dev), opt);
+  g.prefetch = opt.prefetch;
+  g.inject = opt.fault_inject;
   rc = apply_plan("nvfp4_gemm", dev, pl, g, stream);
   if (rc) return rc;
   const char* why = nullptr;
@@ -282,7 +311,10 @@ NVFP4_API int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, con
   g.ldc = ldc;
   g.c_lstride = c_lstride;
   g.status = status_ptr(dev);
-  const GemmPlan pl = gemm_plan(M, N, K, L, true, num_sms_of(dev));
+  const EnvOptions opt = read_env_options();
+  const GemmPlan pl = gemm_plan(M, N, K, L, true, num_sms_of(dev), opt);
+  g.prefetch = opt.prefetch;
+  g.inject = opt.fault_inject;
   rc = apply_plan("nvfp4_dual_gemm", dev, pl, g, stream);
   if (rc) return rc;
   const char* why = nullptr;
@@ -338,4 +370,23 @@ NVFP4_API int nvfp4_scales_from_blocked(const void* blk, void* plain, int rows, 
                                         void* stream) {
   return scale_layout("nvfp4_scales_from_blocked", false, blk, plain, rows, sk, L, plain_row_stride, plain_lstride,
                       blk_lstride, stream);
+}
+
+// Packed-argument forms (include/nvfp4_b200.h): the same calls, one pointer.
+NVFP4_API int nvfp4_gemv_call(const nvfp4_gemv_args* x) {
+  if (!x) return fail(NVFP4_ERR_NULL, "nvfp4_gemv_call: null argument block");
+  return nvfp4_gemv(x->a, x->b, x->sfa_blk, x->sfb_blk, x->c, x->M, x->K, x->L, x->a_lstride, x->b_lstride,
+                    x->sfa_lstride, x->sfb_lstride, x->c_lstride, x->stream);
+}
+
+NVFP4_API int nvfp4_gemm_call(const nvfp4_gemm_args* x) {
+  if (!x) return fail(NVFP4_ERR_NULL, "nvfp4_gemm_call: null argument block");
+  return nvfp4_gemm(x->a, x->b, x->sfa_blk, x->sfb_blk, x->c, x->M, x->N, x->K, x->L, x->a_lstride, x->b_lstride,
+                    x->sfa_lstride, x->sfb_lstride, x->ldc, x->c_lstride, x->stream);
+}
+
+NVFP4_API int nvfp4_dual_gemm_call(const nvfp4_gemm_args* x) {
+  if (!x) return fail(NVFP4_ERR_NULL, "nvfp4_dual_gemm_call: null argument block");
+  return nvfp4_dual_gemm(x->a, x->b, x->b2, x->sfa_blk, x->sfb_blk, x->sfb2_blk, x->c, x->M, x->N, x->K, x->L,
+                         x->a_lstride, x->b_lstride, x->sfa_lstride, x->sfb_lstride, x->ldc, x->c_lstride, x->stream);
 }

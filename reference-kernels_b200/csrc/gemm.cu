@@ -1335,11 +1335,6 @@ static bool make_operand_map(CUtensorMap* map, const void* base, int K2, int row
   return make_tma_3d_u8(map, base, K2, rows, L, K2, lstride, kBKBytes, box_rows);
 }
 
-static int env_int(const char* name) {
-  const char* e = getenv(name);
-  return e ? atoi(e) : 0;
-}
-
 template <int BN, bool kDual>
 static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {
   using Cfg = GemmConfig<BN, kDual>;
@@ -1387,9 +1382,8 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
   p.sk_partial = p.streamk ? reinterpret_cast<float*>(static_cast<uint8_t*>(g.workspace) + kStreamKFlagBytes) : nullptr;
   // Test hook for the bounded-wait path (tests/test_failure_detection.py):
   // the kernel then reports a pipeline timeout instead of hanging.
-  const char* fi = getenv("NVFP4_FAULT_INJECT");
-  p.inject = (fi && fi[0] == '1' && p.splits == 1) ? 1 : 0;
-  p.prefetch = env_int("NVFP4_PREFETCH");
+  p.inject = (g.inject && p.splits == 1) ? 1 : 0;
+  p.prefetch = g.prefetch;
   // Without split: a persistent grid.  With split K: one CTA per (tile,
   // split), the splits of a tile in one cluster.
   const int grid = p.splits == 1 ? (p.num_items < num_sms ? p.num_items : num_sms) : p.num_items;
@@ -1442,16 +1436,16 @@ static int max_active_clusters(int S) {
   return cache[dev][S];
 }
 
-GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms) {
+GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms, const EnvOptions& opt) {
   GemmPlan pl;
-  const int forced_bn = env_int("NVFP4_GEMM_BN");
+  const int forced_bn = opt.gemm_bn;
   pl.bn = (!dual && N % 256 == 0 && forced_bn != 128) ? 256 : 128;
   const int tiles = (M / 128) * (N / pl.bn) * L;
   const int KT = (K + 255) / 256;
   const int ngroups = pl.bn / 32;  // a split owns at least one 32-column group of the tile
   int splits = 1;
   if (tiles < num_sms) splits = num_sms / tiles;
-  const int forced = env_int("NVFP4_SPLITS");
+  const int forced = opt.splits;
   if (forced > 0) splits = forced;
   if (splits > KT / 2) splits = KT / 2;  // at least two K tiles per split
   if (splits > ngroups) splits = ngroups;
@@ -1481,8 +1475,7 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms) {
   // split in clusters; with half the pairs busy, 256x4096x7168, the 1-CTA
   // split is faster).  Splitting K across pairs (stream-K, NVFP4_STREAMK=2)
   // costs a trip of fp32 partial tiles through L2, measured slower.
-  const char* pe = getenv("NVFP4_PAIR");
-  const bool pair_on = pe && pe[0] == '1', pair_off = pe && pe[0] == '0';
+  const bool pair_on = opt.pair == 1, pair_off = opt.pair == 0;
   pl.pair = (!dual && pl.bn == 256 && pl.splits == 1 && M % 256 == 0 && !pair_off) ? 1 : 0;
   if (dual && M % 256 == 0 && !pair_off && (pair_on || 3 * ((M / 256) * (N / 128) * L) >= 2 * (num_sms / 2))) {
     pl.pair = 1;
@@ -1494,7 +1487,7 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms) {
   // tile's K range of the 38 left over.  Used when the busiest worker's K
   // tiles drop by more than 10%.  NVFP4_STREAMK: 1 force on, 2 force the
   // pure form (no whole-tile waves), -1 force off.
-  const int forced_sk = env_int("NVFP4_STREAMK");
+  const int forced_sk = opt.streamk;
   const int wtiles = pl.pair ? (M / 256) * (N / (dual ? 128 : 256)) * L : tiles;
   const int workers = pl.pair ? num_sms / 2 : num_sms;
   if (pl.pair && wtiles < workers && forced_sk == 2) {

@@ -74,6 +74,21 @@ constexpr int kGemvTcMaxCounterBlocks = 16384;
 size_t gemv_tc_workspace_bytes(int M, int K, int L, int num_sms);
 cudaError_t launch_gemv_tc(const GemvTcArgs& g, int num_sms, cudaStream_t stream, const char** why);
 
+// Tuning / test switches from the environment (NVFP4_GEMM_BN, NVFP4_SPLITS,
+// NVFP4_PAIR, NVFP4_STREAMK, NVFP4_PREFETCH, NVFP4_FAULT_INJECT,
+// NVFP4_GEMV_PATH), read in one pass over `environ` per API call (six getenv
+// calls cost ~1.5 us with a hundred-odd variables set).
+struct EnvOptions {
+  int gemm_bn = 0;       // 128 forces 128-wide tiles
+  int splits = 0;        // > 0 forces the 1-CTA kernel's K splits
+  int pair = -1;         // -1 default, 0 never 2-CTA tiles, 1 wherever the shape allows
+  int streamk = 0;       // 0 default (off), -1 off, 1 hybrid, 2 pure
+  int prefetch = 0;      // K tiles of B prefetched into L2
+  int fault_inject = 0;  // test hook: CTA 0 withholds its first A load
+  int gemv_simt = 0;     // NVFP4_GEMV_PATH=simt
+};
+EnvOptions read_env_options();
+
 struct GemmArgs {
   const void *a, *b, *b2, *sfa, *sfb, *sfb2;
   void* c;
@@ -83,6 +98,7 @@ struct GemmArgs {
   int64_t ldc, c_lstride;                          // elements
   int* status;                                     // device status word (bounded-wait timeouts)
   int bn, splits, streamk, streamk_pure, pair;     // from gemm_plan
+  int prefetch, inject;                            // from EnvOptions
   void* workspace;                                 // stream-K partials + flags (zeroed once; left zeroed)
   size_t workspace_bytes;
 };
@@ -94,7 +110,7 @@ struct GemmPlan {
   int pair;     // 1: 2-CTA kernel, 256x256 tiles (plain GEMM, M % 256 == 0, N % 256 == 0, no split)
   size_t workspace_bytes;  // stream-K partial slots + flags; 0 otherwise (split K reduces on chip)
 };
-GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms);
+GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms, const EnvOptions& opt);
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why);
 cudaError_t launch_dual_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why);
 

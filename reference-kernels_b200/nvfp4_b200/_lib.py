@@ -25,6 +25,9 @@ EXPORTS = (
     "nvfp4_quantize",
     "nvfp4_scales_to_blocked",
     "nvfp4_scales_from_blocked",
+    "nvfp4_gemv_call",
+    "nvfp4_gemm_call",
+    "nvfp4_dual_gemm_call",
 )
 
 _P = ctypes.c_void_p
@@ -32,6 +35,22 @@ _I = ctypes.c_int
 _L = ctypes.c_int64
 
 _lib = None
+
+
+class GemvArgs(ctypes.Structure):
+    """nvfp4_gemv_args of include/nvfp4_b200.h."""
+    _fields_ = [("a", _P), ("b", _P), ("sfa_blk", _P), ("sfb_blk", _P), ("c", _P),
+                ("M", ctypes.c_int32), ("K", ctypes.c_int32), ("L", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("a_lstride", _L), ("b_lstride", _L), ("sfa_lstride", _L), ("sfb_lstride", _L), ("c_lstride", _L),
+                ("stream", _P)]
+
+
+class GemmArgs(ctypes.Structure):
+    """nvfp4_gemm_args of include/nvfp4_b200.h (b2 / sfb2_blk used by the dual GEMM only)."""
+    _fields_ = [("a", _P), ("b", _P), ("b2", _P), ("sfa_blk", _P), ("sfb_blk", _P), ("sfb2_blk", _P), ("c", _P),
+                ("M", ctypes.c_int32), ("N", ctypes.c_int32), ("K", ctypes.c_int32), ("L", ctypes.c_int32),
+                ("a_lstride", _L), ("b_lstride", _L), ("sfa_lstride", _L), ("sfb_lstride", _L), ("ldc", _L),
+                ("c_lstride", _L), ("stream", _P)]
 
 
 class Nvfp4Error(RuntimeError):
@@ -65,6 +84,11 @@ def load() -> ctypes.CDLL:
     lib.nvfp4_gemm.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _P]
     lib.nvfp4_dual_gemm.restype = _I
     lib.nvfp4_dual_gemm.argtypes = [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _P]
+    lib.nvfp4_gemv_call.restype = _I
+    lib.nvfp4_gemv_call.argtypes = [ctypes.POINTER(GemvArgs)]
+    for name in ("nvfp4_gemm_call", "nvfp4_dual_gemm_call"):
+        getattr(lib, name).restype = _I
+        getattr(lib, name).argtypes = [ctypes.POINTER(GemmArgs)]
     _lib = lib
     return lib
 

@@ -14,6 +14,7 @@ Reference entry points replaced:
 """
 from __future__ import annotations
 
+import ctypes
 import os
 import weakref
 
@@ -86,9 +87,9 @@ def _gemv_args(data):
     _require(c.dtype == torch.float16 and tuple(c.shape) == (m, 1, l), "c must be fp16 [M, 1, L]")
     sa = _blocked_lstride(sfa_p, m, k // 16, "sfa_permuted")
     sb = _blocked_lstride(sfb_p, sfb_p.shape[2] * 128 if sfb_p.dim() == 6 else 128, k // 16, "sfb_permuted")
-    return _lib.load().nvfp4_gemv, [
+    return _lib.load().nvfp4_gemv_call, _lib.GemvArgs(
         a.data_ptr(), b.data_ptr(), sfa_p.data_ptr(), sfb_p.data_ptr(), c.data_ptr(),
-        m, k, l, a.stride(2), b.stride(2), sa, sb, c.stride(2)]
+        m, k, l, 0, a.stride(2), b.stride(2), sa, sb, c.stride(2), None)
 
 
 def _gemm_args(data):
@@ -102,9 +103,9 @@ def _gemm_args(data):
              "c must be fp16 [M, N, L] with unit column stride")
     sa = _blocked_lstride(sfa_p, m, k // 16, "sfa_permuted")
     sb = _blocked_lstride(sfb_p, n, k // 16, "sfb_permuted")
-    return _lib.load().nvfp4_gemm, [
-        a.data_ptr(), b.data_ptr(), sfa_p.data_ptr(), sfb_p.data_ptr(), c.data_ptr(),
-        m, n, k, l, a.stride(2), b.stride(2), sa, sb, c.stride(0), c.stride(2)]
+    return _lib.load().nvfp4_gemm_call, _lib.GemmArgs(
+        a.data_ptr(), b.data_ptr(), None, sfa_p.data_ptr(), sfb_p.data_ptr(), None, c.data_ptr(),
+        m, n, k, l, a.stride(2), b.stride(2), sa, sb, c.stride(0), c.stride(2), None)
 
 
 def _dual_args(data):
@@ -122,17 +123,20 @@ def _dual_args(data):
     sb1 = _blocked_lstride(sfb1_p, n, k // 16, "sfb1_permuted")
     sb2 = _blocked_lstride(sfb2_p, n, k // 16, "sfb2_permuted")
     _require(sb1 == sb2, "sfb1 and sfb2 must share their batch stride")
-    return _lib.load().nvfp4_dual_gemm, [
+    return _lib.load().nvfp4_dual_gemm_call, _lib.GemmArgs(
         a.data_ptr(), b1.data_ptr(), b2.data_ptr(), sfa_p.data_ptr(), sfb1_p.data_ptr(), sfb2_p.data_ptr(),
-        c.data_ptr(), m, n, k, l, a.stride(2), b1.stride(2), sa, sb1, c.stride(0), c.stride(2)]
+        c.data_ptr(), m, n, k, l, a.stride(2), b1.stride(2), sa, sb1, c.stride(0), c.stride(2), None)
 
 
 # Validated launch arguments per input tuple.  The reference harness calls
-# custom_kernel on the same tuple objects many times; re-validating strides and
-# re-reading seven data pointers costs several microseconds per call.  An entry
-# is used only while every tensor of the tuple is the very object it was built
-# from (weak references), so a recycled id() never hits; a tensor whose storage
-# is swapped in place (Tensor.set_) would not be noticed.
+# custom_kernel on the same tuple objects many times; re-validating strides,
+# re-reading the data pointers and converting 16 scalar ctypes arguments costs
+# several microseconds per call.  Each entry keeps the packed argument block
+# of the C ABI's *_call entry points, so a repeated call only stores the
+# current stream into it.  An entry is used only while every tensor of the
+# tuple is the very object it was built from (weak references), so a recycled
+# id() never hits; a tensor whose storage is swapped in place (Tensor.set_)
+# would not be noticed.
 _CACHE: dict = {}
 _CACHE_MAX = 256
 
@@ -140,20 +144,23 @@ _CACHE_MAX = 256
 def _dispatch(data, build):
     ent = _CACHE.get(id(data))
     if ent is not None:
-        refs, fn, args, dev = ent
+        refs, fn, block, ref, dev = ent
         if all(r() is t for r, t in zip(refs, data)):
-            rc = fn(*args, _raw_stream(dev))
+            block.stream = _raw_stream(dev)
+            rc = fn(ref)
             if rc:
                 _lib.check(rc)
             if _CHECK_STATUS:
                 _post()
             return data[-1]
-    fn, args = build(data)
+    fn, block = build(data)
     dev = data[0].get_device()
-    _lib.check(fn(*args, _raw_stream(dev)))
+    ref = ctypes.byref(block)
+    block.stream = _raw_stream(dev)
+    _lib.check(fn(ref))
     if len(_CACHE) >= _CACHE_MAX:
         _CACHE.pop(next(iter(_CACHE)))
-    _CACHE[id(data)] = (tuple(weakref.ref(t) for t in data), fn, args, dev)
+    _CACHE[id(data)] = (tuple(weakref.ref(t) for t in data), fn, block, ref, dev)
     _post()
     return data[-1]
 

@@ -24,7 +24,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), n
     assert set(_lib.EXPORTS) <= set(names)
-    assert lib.nvfp4_abi_version() == 1
+    assert lib.nvfp4_abi_version() == 2
 
 
 FAKE = 1 << 20  # 16-byte aligned non-null pointer value; never dereferenced
@@ -64,3 +64,46 @@ def test_ops_refuse_cpu_tensors():
     data = inputs.reference_input("gemm", 128, 256, 1, 1, n=128, device="cpu")
     with pytest.raises(_lib.Nvfp4Error, match="CUDA"):
         ops.gemm(data)
+
+
+def test_packed_forms_reject_like_the_scalar_forms():
+    """The *_call entry points take the same arguments in one struct and
+    return the same codes."""
+    import ctypes
+    lib = _lib.load()
+    assert lib.nvfp4_gemm_call(None) == 3
+    g = _lib.GemmArgs(FAKE, FAKE, None, FAKE, FAKE, None, FAKE, 100, 128, 256, 1, 0, 0, 0, 0, 128, 0, None)
+    assert lib.nvfp4_gemm_call(ctypes.byref(g)) == 1
+    g.M, g.a = 128, FAKE + 8
+    assert lib.nvfp4_gemm_call(ctypes.byref(g)) == 2
+    g.a, g.b2, g.sfb2_blk = FAKE, FAKE + 8, FAKE
+    assert lib.nvfp4_dual_gemm_call(ctypes.byref(g)) == 2
+    v = _lib.GemvArgs(FAKE, FAKE, FAKE, FAKE, FAKE, 130, 256, 1, 0, 0, 0, 0, 0, 0, None)
+    assert lib.nvfp4_gemv_call(ctypes.byref(v)) == 1
+
+
+def test_packed_struct_layout_matches_header(tmp_path):
+    """Field offsets of the ctypes mirrors equal those the C compiler gives the
+    header's structs."""
+    import ctypes
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    fields = {"nvfp4_gemv_args": _lib.GemvArgs, "nvfp4_gemm_args": _lib.GemmArgs}
+    lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void) {"]
+    for cname, py in fields.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    got = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l}
+    for cname, py in fields.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py)
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
