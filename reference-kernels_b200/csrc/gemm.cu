@@ -32,6 +32,7 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <cmath>
 #include <cstdlib>
 #include <mutex>
 
@@ -1445,6 +1446,16 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms, const Env
   const int ngroups = pl.bn / 32;  // a split owns at least one 32-column group of the tile
   int splits = 1;
   if (tiles < num_sms) splits = num_sms / tiles;
+  {
+    // Each extra split rank adds ~1 us of DSMEM exchange; each K tile a CTA
+    // runs costs ~0.36 us (same-box measurements on the M=128 / M=256
+    // shapes), so the time a + (S-1) + 0.36*KT/S is least near S = sqrt(0.36*KT):
+    // 2 for K=2048, 3 for K=7168, 5 for K=16384.  Measured: 128x7168x2048
+    // 12.9 -> 10.9 us, 128x4096x7168 17.1 -> 15.2 us against filling the SMs.
+    int model = static_cast<int>(lrint(sqrt(0.36 * KT)));
+    if (model < 1) model = 1;
+    if (splits > model) splits = model;
+  }
   const int forced = opt.splits;
   if (forced > 0) splits = forced;
   if (splits > KT / 2) splits = KT / 2;  // at least two K tiles per split
