@@ -115,6 +115,7 @@ EnvOptions read_env_options() {
     else if ((x = key("PREFETCH"))) o.prefetch = atoi(x);
     else if ((x = key("FAULT_INJECT"))) o.fault_inject = (x[0] == '1');
     else if ((x = key("GEMV_PATH"))) o.gemv_simt = (strcmp(x, "simt") == 0);
+    else if ((x = key("GEMV_CTAS"))) o.gemv_ctas = atoi(x);
   }
   return o;
 }
@@ -154,8 +155,8 @@ NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa_blk, cons
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4_ERR_DEVICE, "nvfp4_gemv: no CUDA device");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const EnvOptions opt = read_env_options();
-  const bool simt = (K % 256 != 0) || opt.gemv_simt ||
-                    gemv_tc_workspace_bytes(M, K, L, num_sms_of(dev)) == 0;
+  const int ctas = (opt.gemv_ctas > 0 && opt.gemv_ctas < num_sms_of(dev)) ? opt.gemv_ctas : num_sms_of(dev);
+  const bool simt = (K % 256 != 0) || opt.gemv_simt || gemv_tc_workspace_bytes(M, K, L, ctas) == 0;
   if (!simt) {
     GemvTcArgs g{};
     g.a = a;
@@ -171,13 +172,13 @@ NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa_blk, cons
     g.sfa_lstride = sfa_lstride;
     g.sfb_lstride = sfb_lstride;
     g.c_lstride = c_lstride;
-    g.workspace_bytes = gemv_tc_workspace_bytes(M, K, L, num_sms_of(dev));
+    g.workspace_bytes = gemv_tc_workspace_bytes(M, K, L, ctas);
     cudaError_t e = cudaSuccess;
     g.workspace = workspace_for(kWsGemv, dev, g.workspace_bytes, s, &e);
     if (!g.workspace) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: workspace: %s", cudaGetErrorString(e));
     g.status = status_ptr(dev);
     const char* why = nullptr;
-    e = launch_gemv_tc(g, num_sms_of(dev), s, &why);
+    e = launch_gemv_tc(g, ctas, s, &why);
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: %s", why ? why : cudaGetErrorString(e));
     return NVFP4_OK;
   }

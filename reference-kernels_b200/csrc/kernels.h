@@ -76,7 +76,7 @@ cudaError_t launch_gemv_tc(const GemvTcArgs& g, int num_sms, cudaStream_t stream
 
 // Tuning / test switches from the environment (NVFP4_GEMM_BN, NVFP4_SPLITS,
 // NVFP4_PAIR, NVFP4_STREAMK, NVFP4_PREFETCH, NVFP4_FAULT_INJECT,
-// NVFP4_GEMV_PATH), read in one pass over `environ` per API call (six getenv
+// NVFP4_GEMV_PATH, NVFP4_GEMV_CTAS), read in one pass over `environ` per API call (six getenv
 // calls cost ~1.5 us with a hundred-odd variables set).
 struct EnvOptions {
   int gemm_bn = 0;       // 128 forces 128-wide tiles
@@ -86,6 +86,7 @@ struct EnvOptions {
   int prefetch = 0;      // K tiles of B prefetched into L2
   int fault_inject = 0;  // test hook: CTA 0 withholds its first A load
   int gemv_simt = 0;     // NVFP4_GEMV_PATH=simt
+  int gemv_ctas = 0;     // > 0 caps the tensor-core GEMV's CTA count (NVFP4_GEMV_CTAS)
 };
 EnvOptions read_env_options();
 
