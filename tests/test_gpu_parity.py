@@ -228,6 +228,7 @@ def test_pair_stream_k_many_contributors(problem, m, n, k, monkeypatch):
 @pytest.mark.parametrize("problem,m,n,k,l", [
     ("gemm", 256, 256, 64, 1), ("gemm", 256, 512, 192, 2), ("gemm", 512, 512, 320, 1), ("gemm", 256, 768, 1856, 1),
     ("gemm", 2048, 2560, 320, 1),  # 160 tiles: no K split, so the 2-CTA kernel runs under "pair"
+    ("gemm", 1664, 3072, 320, 1),  # 156 tiles: stream-K ranges (under "streamk") over a partial last K tile
     ("dual", 256, 256, 448, 1), ("dual", 512, 384, 1344, 1),
 ])
 def test_k_tail(problem, m, n, k, l, kernel, monkeypatch):
