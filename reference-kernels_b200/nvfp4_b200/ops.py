@@ -141,6 +141,13 @@ _CACHE: dict = {}
 _CACHE_MAX = 256
 
 
+def _same_device(data) -> None:
+    dev = data[0].get_device()
+    for i, t in enumerate(data):
+        if isinstance(t, torch.Tensor) and t.is_cuda and t.get_device() != dev:
+            _require(False, f"tuple slot {i} is on cuda:{t.get_device()}, slot 0 on cuda:{dev}")
+
+
 def _dispatch(data, build):
     ent = _CACHE.get(id(data))
     if ent is not None:
@@ -154,6 +161,7 @@ def _dispatch(data, build):
                 _post()
             return data[-1]
     fn, block = build(data)
+    _same_device(data)
     dev = data[0].get_device()
     ref = ctypes.byref(block)
     block.stream = _raw_stream(dev)
