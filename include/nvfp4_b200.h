@@ -56,8 +56,11 @@ const char* nvfp4_last_error(void);
 int nvfp4_abi_version(void);
 
 /* Reads (and optionally clears) the current device's status word, which the
- * GEMM kernels set when a bounded pipeline wait runs out (1..4; 0 = ok).
- * Synchronous.  Returns -1 on a CUDA error. */
+ * tensor-core kernels set when a bounded pipeline wait runs out (non-zero;
+ * 0 = ok).  Synchronous.  Returns -1 on a CUDA error.  Clearing a non-zero
+ * status also zeroes the library's device workspaces (arrival counters,
+ * stream-K flags, partial sums) on that device, which a kernel that gave up
+ * may have left dirty, so the next call starts clean. */
 int nvfp4_device_status(int clear);
 
 /* Batched GEMV: c[m, l] = fp16( sum_k a[m,k,l]*sfa[m,k/16,l] * b[0,k,l]*sfb[0,k/16,l] ).
@@ -89,10 +92,15 @@ int nvfp4_gemv(const void* a, const void* b, const void* sfa_blk, const void* sf
  *   - Requires M % 128 == 0 and K % 256 == 0; a shape whose scratch need
  *     exceeds the array is rejected with NVFP4_ERR_SHAPE and a message.
  *   - The first call on each device looks up the array's device address
- *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
- *   - It calls no cudaMalloc / cudaFree; each call clears the counters with
- *     cudaMemsetAsync on `stream`, then launches the kernel.
+ *     (cudaGetSymbolAddress) with that device current and zeroes the
+ *     arrival counters synchronously; make that first call before any
+ *     stream capture.  The address is kept for the life of the process, so
+ *     do not call it after cudaDeviceReset.
+ *   - It calls no cudaMalloc / cudaFree.  Later calls only launch the
+ *     kernel, which returns every counter it used to zero.
+ *   - A bounded-wait timeout is recorded in the device status word like the
+ *     other entry points'; nvfp4_device_status(1) then also re-zeroes the
+ *     counters.
  *   - All calls share the one array, which keeps the last call's contents:
  *     calls that overlap on the GPU (other streams, other threads) race and
  *     give wrong results. */

@@ -37,7 +37,16 @@ int nvfp4_record_error(int code, const char* fmt, ...) {
 // timeouts here (0 = ok).
 static __device__ int g_status_word;
 
-static int* status_ptr(int dev) {
+namespace nvfp4 {
+// Address of the status word on `dev` (the current device); nullptr if it
+// cannot be looked up.  Shared with the allocation-free GEMV entry point.
+int* device_status_word(int dev);
+void noalloc_scratch_reset(int dev);
+}  // namespace nvfp4
+
+static int* status_ptr(int dev) { return nvfp4::device_status_word(dev); }
+
+int* nvfp4::device_status_word(int dev) {
   static int* ptrs[64] = {nullptr};
   if (dev < 0 || dev >= 64) return nullptr;
   if (!ptrs[dev]) {
@@ -134,9 +143,21 @@ NVFP4_API int nvfp4_device_status(int clear) {
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_status_word, sizeof(int)) != cudaSuccess) return -1;
-  if (clear) {
+  if (clear && v != 0) {
+    // A bounded wait ran out: the kernel that gave up may have left arrival
+    // counters, stream-K flags or partial sums in the shared workspaces.  Wait
+    // for the device, then zero every workspace of this device (and the
+    // allocation-free GEMV's scratch) so that the next call starts clean.
+    cudaDeviceSynchronize();
+    {
+      std::lock_guard<std::mutex> lock(g_ws_mutex);
+      for (int kind = 0; kind < 2; ++kind)
+        if (dev >= 0 && dev < 64 && g_ws[kind][dev].ptr) cudaMemset(g_ws[kind][dev].ptr, 0, g_ws[kind][dev].bytes);
+    }
+    nvfp4::noalloc_scratch_reset(dev);
     const int zero = 0;
     cudaMemcpyToSymbol(g_status_word, &zero, sizeof(int));
+    cudaDeviceSynchronize();
   }
   return v;
 }
@@ -177,6 +198,7 @@ NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa_blk, cons
     g.workspace = workspace_for(kWsGemv, dev, g.workspace_bytes, s, &e);
     if (!g.workspace) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: workspace: %s", cudaGetErrorString(e));
     g.status = status_ptr(dev);
+    g.inject = opt.fault_inject;
     const char* why = nullptr;
     e = launch_gemv_tc(g, ctas, s, &why);
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: %s", why ? why : cudaGetErrorString(e));

@@ -918,7 +918,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       uint32_t phase = 0;
       WorkIter wi(p, pair_id, npairs);
       int t, k0, k1;
-      while (!abort_flag && wi.next(p, KT, t, k0, k1)) {
+      for (bool first = true; !abort_flag && wi.next(p, KT, t, k0, k1); first = false) {
         int mb, nb, l;
         tile_coords(p, t, mb, nb, l);
         const int arow = mb * 256 + static_cast<int>(rank) * 128;
@@ -939,7 +939,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           uint8_t* st = smem + stage * kStage;
           const uint32_t bar0 = map_peer(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], kTx);
-          tma_load_3d_pair(st, &tm_a, bar0, kt * kBKBytes, arow, l, pol_a);
+          if (!(p.inject && blockIdx.x == 0 && first && kt == k0))
+            tma_load_3d_pair(st, &tm_a, bar0, kt * kBKBytes, arow, l, pol_a);
           tma_load_3d_pair(st + kA, bmap, bar0, kt * kBKBytes, brow, l, pol_b);
           // Scales into this CTA's own shared memory, on its own barrier: SFA
           // of its 128 rows, SFB of both 128-row blocks of the tile's N.
@@ -1382,8 +1383,10 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
   p.sk_flag = static_cast<int*>(g.workspace);
   p.sk_partial = p.streamk ? reinterpret_cast<float*>(static_cast<uint8_t*>(g.workspace) + kStreamKFlagBytes) : nullptr;
   // Test hook for the bounded-wait path (tests/test_failure_detection.py):
-  // the kernel then reports a pipeline timeout instead of hanging.
-  p.inject = (g.inject && p.splits == 1) ? 1 : 0;
+  // the kernel then reports a pipeline timeout instead of hanging.  With
+  // split K the other CTAs of CTA 0's cluster finish their main loops and
+  // wait at the cluster barrier until CTA 0's bounded waits have run out.
+  p.inject = g.inject ? 1 : 0;
   p.prefetch = g.prefetch;
   // Without split: a persistent grid.  With split K: one CTA per (tile,
   // split), the splits of a tile in one cluster.
@@ -1577,6 +1580,7 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
   p.num_tiles = p.tiles_m * p.tiles_n * g.L;
   p.group_m = p.tiles_m < 8 ? p.tiles_m : 8;
   p.status = g.status;
+  p.inject = g.inject ? 1 : 0;
   p.splits = 1;
   p.num_items = p.num_tiles;
   p.streamk = (g.streamk && g.workspace) ? 1 : 0;

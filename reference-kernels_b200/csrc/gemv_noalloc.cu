@@ -33,6 +33,10 @@ void* g_scratch_addr[64] = {nullptr};
 int g_num_sms[64] = {0};
 std::mutex g_setup_mutex;
 
+// First call on a device: look up the array's device address and the SM
+// count, and zero the arrival counters once (synchronously, which is why the
+// first call must not be inside a stream capture).  Later calls rely on the
+// kernel leaving every counter it used back at zero.
 cudaError_t setup_device(int dev) {
   std::lock_guard<std::mutex> lock(g_setup_mutex);
   if (g_scratch_addr[dev]) return cudaSuccess;
@@ -42,12 +46,26 @@ cudaError_t setup_device(int dev) {
   int n = 0;
   e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
+  e = cudaMemset(ptr, 0, sizeof(int) * kGemvTcMaxCounterBlocks);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return e;
   g_num_sms[dev] = n > 0 ? n : 148;
   g_scratch_addr[dev] = ptr;
   return cudaSuccess;
 }
 
 }  // namespace
+
+int* device_status_word(int dev);  // capi.cu
+
+// Called by nvfp4_device_status(clear) after a recorded timeout: a GEMV that
+// gave up may have left its arrival counters non-zero.
+void noalloc_scratch_reset(int dev) {
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  if (dev >= 0 && dev < 64 && g_scratch_addr[dev])
+    cudaMemset(g_scratch_addr[dev], 0, sizeof(int) * kGemvTcMaxCounterBlocks);
+}
 }  // namespace nvfp4
 
 using namespace nvfp4;
@@ -80,16 +98,19 @@ extern "C" __attribute__((visibility("default"))) int nvfp4_gemv_noalloc(
     return noalloc_fail(NVFP4_ERR_CUDA, "nvfp4_gemv_noalloc: cudaGetSymbolAddress of the scratch array failed: %s",
                         cudaGetErrorString(e));
   const size_t need = gemv_tc_workspace_bytes(M, K, L, g_num_sms[dev]);
-  if (need == 0 || need > kNoAllocScratchBytes)
+  if (need == 0)
+    return noalloc_fail(NVFP4_ERR_SHAPE,
+                        "nvfp4_gemv_noalloc: M=%d L=%d gives %lld 128-row blocks, more than the %d arrival "
+                        "counters of the fixed scratch array",
+                        M, L, static_cast<long long>(M / 128) * L, kGemvTcMaxCounterBlocks);
+  if (need > kNoAllocScratchBytes)
     return noalloc_fail(NVFP4_ERR_SHAPE,
                         "nvfp4_gemv_noalloc: M=%d K=%d L=%d needs %zu bytes of scratch, more than the fixed %zu",
                         M, K, L, need, kNoAllocScratchBytes);
+  int* status = device_status_word(dev);
+  if (!status)
+    return noalloc_fail(NVFP4_ERR_CUDA, "nvfp4_gemv_noalloc: cannot look up the device status word");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The arrival counters must start at zero; the kernel leaves them zeroed,
-  // but clear them every call so an interrupted earlier call cannot leak in.
-  e = cudaMemsetAsync(g_scratch_addr[dev], 0, sizeof(int) * kGemvTcMaxCounterBlocks, s);
-  if (e != cudaSuccess)
-    return noalloc_fail(NVFP4_ERR_CUDA, "nvfp4_gemv_noalloc: clearing counters: %s", cudaGetErrorString(e));
   GemvTcArgs g{};
   g.a = a;
   g.b = b;
@@ -106,7 +127,7 @@ extern "C" __attribute__((visibility("default"))) int nvfp4_gemv_noalloc(
   g.c_lstride = c_lstride;
   g.workspace = g_scratch_addr[dev];
   g.workspace_bytes = kNoAllocScratchBytes;
-  g.status = nullptr;
+  g.status = status;
   const char* why = nullptr;
   e = launch_gemv_tc(g, g_num_sms[dev], s, &why);
   if (e != cudaSuccess)

@@ -67,6 +67,7 @@ struct GemvTcParams {
   int64_t sfa_lstride, sfb_lstride, c_lstride;
   int units, kt_per_block, blocks_per_l, slots;
   int* status;
+  int inject;  // test hook: CTA 0 withholds its first A load
 };
 
 // First unit of CTA `c` when `units` are split over `ctas` CTAs.
@@ -173,7 +174,8 @@ __global__ void __launch_bounds__(gemvtc::kThreads, 1)
         }
         uint8_t* st = smem + stage * kStageBytes;
         mbar_arrive_expect_tx(&full[stage], kTxBytes);
-        tma_load_4d(st, &tm_a, &full[stage], 0, mb * kBM, kt * SUB, l, pol_stream);
+        if (!(p.inject && blockIdx.x == 0 && u == u0))
+          tma_load_4d(st, &tm_a, &full[stage], 0, mb * kBM, kt * SUB, l, pol_stream);
         tma_load_4d(st + C::kA, &tm_b, &full[stage], 0, 0, kt * SUB, l, pol_keep);
         bulk_load(st + C::kA + C::kB,
                   p.sfa + l * p.sfa_lstride + static_cast<int64_t>(mb) * p.K * 8 + kt * C::kSf, C::kSf,
@@ -411,6 +413,7 @@ static cudaError_t launch_sub(const GemvTcArgs& g, int num_sms, cudaStream_t str
   p.counters = static_cast<int*>(g.workspace);
   p.ws = reinterpret_cast<float*>(p.counters + kGemvTcMaxCounterBlocks);
   p.status = g.status;
+  p.inject = g.inject;
   return launch_pdl(gemv_tc_kernel<SUB>, dim3(grid), dim3(kThreads), C::kSmemBytes, stream, 1, ta, tb, p);
 }
 

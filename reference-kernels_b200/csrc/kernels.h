@@ -67,6 +67,7 @@ struct GemvTcArgs {
   void* workspace;                                          // zero-initialised counters + partial sums
   size_t workspace_bytes;
   int* status;
+  int inject;  // test hook: CTA 0 withholds its first A load (its pipeline waits then run out)
 };
 // Row blocks (M/128 * L) the tensor-core GEMV can track; larger calls use the SIMT GEMV.
 constexpr int kGemvTcMaxCounterBlocks = 16384;

@@ -141,18 +141,27 @@ _CACHE: dict = {}
 _CACHE_MAX = 256
 
 
+_current_device = torch._C._cuda_getDevice
+
+
 def _same_device(data) -> None:
+    """Every tensor on one device, and that device the current one: the
+    library takes its workspace, status word and tensor-map context from the
+    current device, and the stream from the tensors' device."""
     dev = data[0].get_device()
     for i, t in enumerate(data):
         if isinstance(t, torch.Tensor) and t.is_cuda and t.get_device() != dev:
             _require(False, f"tuple slot {i} is on cuda:{t.get_device()}, slot 0 on cuda:{dev}")
+    _require(dev == _current_device(),
+             f"the tensors are on cuda:{dev} but cuda:{_current_device()} is current; "
+             f"call inside torch.cuda.device({dev})")
 
 
 def _dispatch(data, build):
     ent = _CACHE.get(id(data))
     if ent is not None:
         refs, fn, block, ref, dev = ent
-        if all(r() is t for r, t in zip(refs, data)):
+        if all(r() is t for r, t in zip(refs, data)) and dev == _current_device():
             block.stream = _raw_stream(dev)
             rc = fn(ref)
             if rc:

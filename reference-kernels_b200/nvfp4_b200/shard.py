@@ -40,6 +40,27 @@ def shard_tuple(problem: str, data, world: int, rank: int):
     raise ValueError(problem)
 
 
+def _dense(t):
+    """A copy of `t` in the reference's storage order: operands / C
+    [rows, cols, L] over contiguous (L, rows, cols); blocked scales
+    (32, 4, rb, 4, kk, L) over contiguous (L, rb, kk, 32, 4, 4)."""
+    if t.dim() == 3:
+        return t.permute(2, 0, 1).contiguous().permute(1, 2, 0)
+    if t.dim() == 6:
+        return t.permute(5, 2, 4, 0, 1, 3).contiguous().permute(3, 4, 1, 5, 2, 0)
+    return t.contiguous()
+
+
+def dense_shard_tuple(problem: str, data, world: int, rank: int):
+    """`shard_tuple` with every sliced tensor copied into its own dense
+    buffer, so the rank's inputs and output are laid out exactly as the
+    reference's generate_input lays out a problem of the shard's size (one
+    contiguous run per tensor: a host <-> device copy is a single DMA)."""
+    if world == 1:
+        return data
+    return tuple(_dense(t) for t in shard_tuple(problem, data, world, rank))
+
+
 def output_slice(problem: str, shape, world: int, rank: int):
     """Index expression of the rank's part of C ([M, N, L])."""
     if problem == "gemv":

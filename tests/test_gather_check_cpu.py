@@ -1,6 +1,6 @@
 """bench.py's multi-GPU correctness check (gather_check) on CPU with gloo
 ranks: the ranks' C slices — of unequal widths, so the all-gather pads — are
-assembled and compared with rank 0's whole-problem result; a wrong element in
+assembled and compared with rank 0's expected whole-problem result; a wrong element in
 one rank's slice is caught."""
 import os
 import socket
@@ -27,11 +27,6 @@ def _pattern(shape):
     return (i % 997).to(torch.float16)
 
 
-def _whole_problem(data):
-    c = data[-1]
-    c.copy_(_pattern(tuple(c.shape)))
-
-
 def _worker(rank, world, port, problem, m, n, k, corrupt, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -39,11 +34,12 @@ def _worker(rank, world, port, problem, m, n, k, corrupt, q):
         import bench
         data = inputs.baseline_input(problem, m, k, 1, 5, n=None if problem == "gemv" else n, device="cpu")
         c = data[-1]
-        sl = shard.output_slice(problem, tuple(c.shape), world, rank)
-        c[sl] = _pattern(tuple(c.shape))[sl]  # this rank's shard result
+        shape = tuple(c.shape)
+        sl = shard.output_slice(problem, shape, world, rank)
+        mine = _pattern(shape)[sl].clone()  # this rank's shard result
         if corrupt and rank == world - 1:
-            c[sl][0, 0, 0] += 1
-        res = bench.gather_check(problem, data, _whole_problem, world, rank, dist)
+            mine[0, 0, 0] += 1
+        res = bench.gather_check(problem, shape, mine, lambda: _pattern(shape), world, rank, dist)
         if rank == 0:
             q.put(("ok", res))
     except Exception as e:

@@ -4,9 +4,8 @@ is copied into a flat working directory and imported as the module
 ``submission``; custom_kernel is called on deep clones of generate_input's
 tuple (clone() keeps the permuted strides), on 50 inputs with distinct seeds,
 and every output is checked with the reference's tolerance against
-torch._scaled_mm (ref_kernel's arithmetic).  The reference's own harness
-files are not present on the GPU boxes; INTEGRATION.md describes running the
-real eval.py."""
+torch._scaled_mm (ref_kernel's arithmetic).  It needs no copy of the
+reference; tests/test_reference_harness.py runs the reference's real harness."""
 import importlib.util
 import os
 import shutil

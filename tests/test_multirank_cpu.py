@@ -92,3 +92,25 @@ def test_shard_bounds_balanced():
     b = [shard.shard_bounds(7168, 8, r) for r in range(8)]
     assert b[0] == (0, 896) and b[-1] == (7168 - 896, 7168)
     assert all(hi - lo in (0, 896) for lo, hi in b)
+
+
+@pytest.mark.parametrize("problem,m,n,k,l", CASES)
+def test_dense_shards_match_views_and_are_dense(problem, m, n, k, l):
+    """dense_shard_tuple: equal values to the shard views, each tensor one
+    dense run in the reference's storage order (so a pinned host buffer of
+    the same strides copies in one DMA)."""
+    world = 2
+    if problem == "gemv" and m // 128 < world or problem != "gemv" and n // 128 < world:
+        pytest.skip("fewer 128-blocks than ranks")
+    data = inputs.reference_input(problem, m, k, l, 3, n=None if problem == "gemv" else n, device="cpu")
+    for r in range(world):
+        views = shard.shard_tuple(problem, data, world, r)
+        dense = shard.dense_shard_tuple(problem, data, world, r)
+        for v, d in zip(views, dense):
+            assert v.shape == d.shape
+            assert torch.equal(v.view(torch.uint8) if v.element_size() == 1 else v,
+                               d.view(torch.uint8) if d.element_size() == 1 else d)
+            # dense: the strides are a permutation of a contiguous layout
+            assert d.is_contiguous() or d.permute(*sorted(range(d.dim()), key=lambda i: -d.stride(i))).is_contiguous()
+        a = dense[0]
+        assert a.stride() == (a.shape[1], 1, a.shape[0] * a.shape[1])
