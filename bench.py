@@ -693,6 +693,7 @@ def main():
                          "per shape) and exit")
     ap.add_argument("--suite-only", default=None, help="comma-separated problems for --suite")
     ap.add_argument("--cpu-seconds", type=float, default=5.0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg (tuning runs)")
     ap.add_argument("--ref-seconds", type=float, default=60.0,
                     help="time budget of the reference arm's timed passes")
     for d in "mnkl":
@@ -724,7 +725,7 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     ctx = Ctx(world, rank, local, dev, dist)
 
-    line = measure(cfg, args, ctx, args.steps, with_cpu=True)
+    line = measure(cfg, args, ctx, args.steps, with_cpu=not args.no_cpu)
     if args.all_configs:
         per = {}
         for name in PER_CONFIG:
@@ -732,7 +733,7 @@ def main():
             # the 16384^3 GEMM runs ~2 ms per step on one GPU: fewer steps keep
             # its timed region near a second
             steps = min(args.steps, 50) if name == "gemm_square" else args.steps
-            per[name] = measure(c, args, ctx, steps, with_cpu=True)
+            per[name] = measure(c, args, ctx, steps, with_cpu=not args.no_cpu)
         line["per_config"] = per
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -125,6 +125,7 @@ EnvOptions read_env_options() {
     else if ((x = key("FAULT_INJECT"))) o.fault_inject = (x[0] == '1');
     else if ((x = key("GEMV_PATH"))) o.gemv_simt = (strcmp(x, "simt") == 0);
     else if ((x = key("GEMV_CTAS"))) o.gemv_ctas = atoi(x);
+    else if ((x = key("B_EVICT"))) o.b_evict = atoi(x);
   }
   return o;
 }
@@ -293,6 +294,7 @@ NVFP4_API int nvfp4_gemm(const void* a, const void* b, const void* sfa_blk, cons
   const GemmPlan pl = gemm_plan(M, N, K, L, false, num_sms_of(dev), opt);
   g.prefetch = opt.prefetch;
   g.inject = opt.fault_inject;
+  g.b_evict = opt.b_evict >= 0 ? opt.b_evict : pl.b_evict;
   rc = apply_plan("nvfp4_gemm", dev, pl, g, stream);
   if (rc) return rc;
   const char* why = nullptr;
@@ -338,6 +340,7 @@ NVFP4_API int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, con
   const GemmPlan pl = gemm_plan(M, N, K, L, true, num_sms_of(dev), opt);
   g.prefetch = opt.prefetch;
   g.inject = opt.fault_inject;
+  g.b_evict = opt.b_evict >= 0 ? opt.b_evict : pl.b_evict;
   rc = apply_plan("nvfp4_dual_gemm", dev, pl, g, stream);
   if (rc) return rc;
   const char* why = nullptr;

@@ -62,12 +62,12 @@ __device__ unsigned long long g_gemm_trace[1024 * 32];
     trace[slot] += clock64() - _t0;          \
     _r;                                      \
   })
-#define TRACE_DECL unsigned long long trace[16] = {}; const long long trace_t0 = clock64()
+#define TRACE_DECL unsigned long long trace[20] = {}; const long long trace_t0 = clock64()
 #define TRACE_TOTAL(slot) trace[slot] = clock64() - trace_t0
 #define TRACE_FLUSH()                                                             \
   do {                                                                            \
     if (lane == 0)                                                                \
-      for (int _i = 0; _i < 16; ++_i)                                             \
+      for (int _i = 0; _i < 20; ++_i)                                             \
         if (trace[_i]) g_gemm_trace[blockIdx.x * 32 + _i] = trace[_i];             \
   } while (0)
 #else
@@ -91,10 +91,24 @@ constexpr int kSfStageBytes = kSfBlockBytes * (kBK / kMmaK);  // 2 KB per operan
 // Scale copiers of the 1-CTA kernel: four warps (6..9), one per TMEM lane
 // quarter, write the scales with tcgen05.st.
 constexpr int kCopiers = 4;
-constexpr int kThreads = 192 + 32 * kCopiers;
+// TMA producers: warp 0 and warps 10.. .  A thread that waits on an mbarrier
+// between its bulk copies keeps only about one copy in flight (measured: one
+// producer thread streams ~60 GB/s into an SM whatever the ring depth, four
+// reach ~130 GB/s per SM with every SM loading), so the K tiles are dealt
+// round-robin to kProducers warps, each waiting only for its own stages.
+#ifndef NVFP4_PRODUCERS
+#define NVFP4_PRODUCERS 4
+#endif
+constexpr int kProducers = NVFP4_PRODUCERS;
+constexpr int kThreads = 192 + 32 * kCopiers + 32 * (kProducers - 1);
 // The 2-CTA kernel: four scale-writer warps per CTA as well.
 constexpr int kPairCopiers = 4;
-constexpr int kPairThreads = 192 + 32 * kPairCopiers;
+constexpr int kPairThreads = 192 + 32 * kPairCopiers + 32 * (kProducers - 1);
+
+// Producer index of a warp (0 .. kProducers-1), or -1.
+__device__ __forceinline__ int producer_index(int warp) {
+  return warp == 0 ? 0 : (warp >= 10 && warp < 9 + kProducers) ? warp - 9 : -1;
+}
 
 template <int BN, bool kDual>
 struct GemmConfig {
@@ -130,6 +144,7 @@ struct GemmParams {
                 // `splits` CTAs, one item per CTA, cluster = tile.
   int num_items;
   int prefetch;  // K tiles ahead to prefetch B into L2 (0 = off)
+  int b_evict;   // L2 policy of B loads: 0 evict_first, 1 evict_normal, 2 evict_last
   // Stream-K (splits == 1 only): the tiles x K-tiles "units", in tile-major
   // order, are cut into gridDim.x equal contiguous ranges, one per CTA.  A CTA
   // whose range starts inside a tile (its first segment) writes that partial
@@ -362,13 +377,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   TRACE_CLOCK(14);
   bool split_ready = false;  // epilogue threads: this CTA's split partial is in TMEM
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (producer_index(warp) >= 0) {
+    // ------------------------------------------------------------ producers
+    // K tile g of this CTA's sequence (over all its work items) goes to
+    // producer g % kProducers, in stage g % S.
+    const int pidx = producer_index(warp);
     if (lane == 0) {
       const uint64_t pol_a = policy_evict_last();
-      const uint64_t pol_b = policy_evict_first();
-      int stage = 0;
-      uint32_t phase = 0;
+      const uint64_t pol_b = policy_of(p.b_evict);
+      int g = 0;
       WorkIter wi(p, blockIdx.x, gridDim.x);
       int t, k0, k1, item = 0;
       for (; !abort_flag && wi.next(p, KT, t, k0, k1); ++item) {
@@ -378,7 +395,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* sfb_src = p.sfb + l * p.sfb_lstride + static_cast<int64_t>(nb) * (BN / 128) * p.K * 8;
         const uint8_t* sfb2_src =
             kDual ? p.sfb2 + l * p.sfb2_lstride + static_cast<int64_t>(nb) * (BN / 128) * p.K * 8 : nullptr;
-        for (int kt = k0; kt < k1; ++kt) {
+        for (int kt = k0; kt < k1; ++kt, ++g) {
+          if (g % kProducers != pidx) continue;
+          const int stage = g % S;
+          const uint32_t phase = (g / S) & 1;
           if (!TRW(3, mbar_wait(&empty[stage], phase ^ 1))) {
             set_status(p.status, kStatusTimeoutEmpty);
             abort_flag = 1;
@@ -413,10 +433,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.prefetch && kt + p.prefetch < k1) {
             tma_prefetch_3d(&tm_b, (kt + p.prefetch) * kBKBytes, nb * BN, l);
             if (kDual) tma_prefetch_3d(&tm_b2, (kt + p.prefetch) * kBKBytes, nb * BN, l);
-          }
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1;
           }
         }
       }
@@ -488,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(drain);
       mbar_wait(drain, 0);
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 6 && warp <= 9) {
     // ------------------------------------------------------------ scale copiers
     // Warps 6..9, one per TMEM lane quarter (warp % 4).  Per stage every
     // warp reads the stage's 512-byte scale blocks from shared memory (lane
@@ -781,7 +797,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // arrive on the leader's sf_ready barrier; MMA completion is multicast to
 // both CTAs' empty / accumulator barriers.  No load uses cluster multicast.
 namespace pair {
-constexpr int kStages = 5;
+constexpr int kStages = 4;
 constexpr int kA = kBM * kBKBytes;       // 16 KB: this CTA's 128 rows of A
 constexpr int kB = 128 * kBKBytes;       // 16 KB: this CTA's 128 rows of B
 constexpr int kSfa = kSfStageBytes;      // 2 KB
@@ -797,7 +813,14 @@ constexpr int kFixBufs = 8;          // stream-K finaliser ring: 8 x 16 KB in th
 constexpr int kFixChunk = 16 * 1024;  // one (contributor, 32-column group) of a partial slot
 constexpr int kMaxContrib = 16;       // contributors per finalised tile
 static_assert(kFixBufs * kFixChunk <= kStages * kStage, "fix-up ring fits in the stage area");
-constexpr int kSmem = 1024 + kStages * kStage + 256;
+// Epilogue staging for whole tiles: this CTA's 128 x 256 fp16 outputs as four
+// 64-column boxes of 128 rows x 128 bytes (128-byte swizzle), written from
+// TMEM by the epilogue warps and stored to C by TMA while the next tile's
+// MMAs run (the accumulator is released as soon as TMEM has been read).
+constexpr int kOutBox = 128 * 128;
+constexpr int kOut = 4 * kOutBox;
+constexpr int kSmem = 1024 + kStages * kStage + kOut + 256;
+static_assert(kSmem <= 227 * 1024, "shared memory budget");
 }  // namespace pair
 
 __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t mbar_cluster, int x,
@@ -857,13 +880,15 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 template <bool kDual>
 __global__ void __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                     const __grid_constant__ CUtensorMap tm_b2, const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_c,
+                     const GemmParams p) {
   if (threadIdx.x == 0) TRACE_STAMP(8);
   using namespace pair;
   constexpr int S = kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kStage);
+  uint8_t* outbuf = smem + S * kStage;  // epilogue staging (kOut bytes, 1024-aligned)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(outbuf + kOut);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* sf_ready = bars + 2 * S;
@@ -896,6 +921,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     fence_barrier_init();
     prefetch_tensormap(&tm_a);
     prefetch_tensormap(kDual && rank ? &tm_b2 : &tm_b);
+    prefetch_tensormap(&tm_c);
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, kTmemCols);
   tc_fence_before();
@@ -909,13 +935,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (threadIdx.x == 0) TRACE_STAMP(9);
   TRACE_CLOCK(14);
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer (both CTAs)
+  if (producer_index(warp) >= 0) {
+    // ------------------------------------------------------------ producers (both CTAs)
+    // K tile g of the pair's sequence goes to producer g % kProducers, stage g % S.
+    const int pidx = producer_index(warp);
     if (lane == 0) {
       const uint64_t pol_a = policy_evict_last();
-      const uint64_t pol_b = policy_evict_first();
-      int stage = 0;
-      uint32_t phase = 0;
+      const uint64_t pol_b = policy_of(p.b_evict);
+      int g = 0;
       WorkIter wi(p, pair_id, npairs);
       int t, k0, k1;
       for (bool first = true; !abort_flag && wi.next(p, KT, t, k0, k1); first = false) {
@@ -930,7 +957,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const uint8_t* sfb_src0 = p.sfb + l * p.sfb_lstride + static_cast<int64_t>(kDual ? nb : 2 * nb) * p.K * 8;
         const uint8_t* sfb_src1 = kDual ? p.sfb2 + l * p.sfb2_lstride + static_cast<int64_t>(nb) * p.K * 8
                                         : sfb_src0 + static_cast<int64_t>(p.K) * 8;
-        for (int kt = k0; kt < k1; ++kt) {
+        for (int kt = k0; kt < k1; ++kt, ++g) {
+          if (g % kProducers != pidx) continue;
+          const int stage = g % S;
+          const uint32_t phase = (g / S) & 1;
           if (!TRW(3, mbar_wait(&empty[stage], phase ^ 1))) {
             set_status(p.status, kStatusTimeoutEmpty);
             abort_flag = 1;
@@ -950,10 +980,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           bulk_load(st + kA + kB + kSfa, sfb_src0 + kt * kSfStageBytes, sf_bytes, &sf_full[stage], pol_b);
           bulk_load(st + kA + kB + kSfa + kSfStageBytes, sfb_src1 + kt * kSfStageBytes, sf_bytes, &sf_full[stage],
                     pol_b);
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1;
-          }
         }
       }
     }
@@ -967,7 +993,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       WorkIter wi(p, pair_id, npairs);
       int t, k0, k1;
       while (!abort_flag && ok && wi.next(p, KT, t, k0, k1)) {
-        if (!mbar_wait(acc_empty, acc_phase ^ 1)) {
+        if (!TRW(16, mbar_wait(acc_empty, acc_phase ^ 1))) {
           set_status(p.status, kStatusTimeoutAccEmpty);
           abort_flag = 1;
           break;
@@ -981,6 +1007,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             break;
           }
           tc_fence_after();
+          TRACE_ISSUE_BEGIN;
           const uint32_t st = smem_u32(smem + stage * kStage);
           const uint32_t sfc = tmem_base + sf_col0 + stage * kSfCols;
           const int nkk = ksteps(p.K, kt);
@@ -991,6 +1018,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                           desc_kmajor_sw128(st + kA + kk * (kMmaK / 2)), idesc, sfc + 4 * kk, sfc + 16 + 8 * kk,
                           (kt != k0 || kk != 0) ? 1u : 0u);
           tc_commit_pair_mc(&empty[stage], 0x3);
+          TRACE_ISSUE_END;
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -1004,7 +1032,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       tc_commit_pair(drain);
       mbar_wait(drain, 0);
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 6 && warp <= 9) {
     // ------------------------------------------------------------ scale writers (both CTAs)
     // Warps 6..9 of each CTA, one per TMEM lane quarter, write the CTA's own
     // scale runs into its own TMEM with tcgen05.st, in the layout
@@ -1062,8 +1090,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     while (wi.next(p, KT, t, k0, k1)) {
       int mb, nb, l;
       tile_coords(p, t, mb, nb, l);
-      if (!__all_sync(0xffffffffu, TRW(6, mbar_wait(acc_full, acc_phase)))) {
-        if (lane == 0) set_status(p.status, kStatusTimeoutAccFull);
+      // All four epilogue warps agree (named barrier 1) before any of them
+      // goes on, so none is ever left alone at a named barrier below.
+      if (!epi_all(TRW(6, mbar_wait(acc_full, acc_phase)))) {
+        if (threadIdx.x == 64) set_status(p.status, kStatusTimeoutAccFull);
         abort_flag = 1;
         break;
       }
@@ -1072,11 +1102,22 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const int row = mb * 256 + static_cast<int>(rank) * 128 + rloc;
       __half* crow = p.c + l * p.c_lstride + static_cast<int64_t>(row) * p.ldc + static_cast<int64_t>(nb) * (kDual ? 128 : 256);
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+#ifdef NVFP4_TRACE
+      const long long epi_t0 = clock64();
+#endif
       if (!p.streamk) {
-        // Whole tile (the common case), kept compact and ahead of the
-        // stream-K paths.
+        // Whole tile (the common case): TMEM -> fp16 -> swizzled staging in
+        // shared memory; the accumulator is released as soon as TMEM has been
+        // read, and one thread stores the staged boxes to C with TMA while
+        // the next tile's MMAs run.  The previous tile's stores must have
+        // finished reading the staging buffer first.
+        if (threadIdx.x == 64) bulk_wait_group_read0();
+        epi_bar();
+        constexpr int kChunks = kDual ? 4 : 8;  // 32-column chunks of this CTA's output rows
+        uint8_t* srow = outbuf + rloc * 128;
+        const int sw = rloc & 7;
 #pragma unroll 1
-        for (int o = 0; o < (kDual ? 4 : 8); ++o) {
+        for (int o = 0; o < kChunks; ++o) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tacc + o * 32, r);
           if (kDual) {
@@ -1089,10 +1130,38 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           } else {
             tmem_wait_ld();
           }
-          store_half_row32(crow + o * 32, r);
+          // 32 columns = 64 bytes = four 16-byte units of the row in box
+          // o / 2, units 4 * (o % 2) .. +3, at unit position u ^ (row % 8).
+          uint8_t* box = srow + (o >> 1) * kOutBox;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 v;
+            __half2 h0 = __floats2half2_rn(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
+            __half2 h1 = __floats2half2_rn(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
+            __half2 h2 = __floats2half2_rn(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
+            __half2 h3 = __floats2half2_rn(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
+            v.x = *reinterpret_cast<uint32_t*>(&h0);
+            v.y = *reinterpret_cast<uint32_t*>(&h1);
+            v.z = *reinterpret_cast<uint32_t*>(&h2);
+            v.w = *reinterpret_cast<uint32_t*>(&h3);
+            const int u = 4 * (o & 1) + j;
+            *reinterpret_cast<uint4*>(box + ((u ^ sw) << 4)) = v;
+          }
         }
         tc_fence_before();
         mbar_arrive_cluster_relaxed(acc_empty0);
+        fence_proxy_async_smem();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const int y = mb * 256 + static_cast<int>(rank) * 128;
+          const int x = nb * (kDual ? 128 : 256) * 2;  // bytes
+#pragma unroll
+          for (int bx = 0; bx < kChunks / 2; ++bx) tma_store_3d(&tm_c, outbuf + bx * kOutBox, x + bx * 128, y, l);
+          bulk_commit_group();
+        }
+#ifdef NVFP4_TRACE
+        trace[17] += clock64() - epi_t0;
+#endif
       } else if (k0 > 0) {
         // Contributor: this CTA's 128 rows of the partial tile to its slot
         // ([column group][float4 index][row][4] floats), then its flag.
@@ -1212,6 +1281,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (warp == 2) TRACE_TOTAL(7);
   if (warp <= 2 || warp == 6) TRACE_FLUSH();
 #endif
+  // TMA stores of C issued by this CTA must be complete before it exits.
+  if (threadIdx.x == 64) bulk_wait_group0();
   // The leader's MMAs read both CTAs' shared memory and write both TMEMs:
   // neither CTA frees TMEM or exits before the pair's work has drained.
   tc_fence_before();
@@ -1388,6 +1459,7 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
   // wait at the cluster barrier until CTA 0's bounded waits have run out.
   p.inject = g.inject ? 1 : 0;
   p.prefetch = g.prefetch;
+  p.b_evict = g.b_evict;
   // Without split: a persistent grid.  With split K: one CTA per (tile,
   // split), the splits of a tile in one cluster.
   const int grid = p.splits == 1 ? (p.num_items < num_sms ? p.num_items : num_sms) : p.num_items;
@@ -1476,6 +1548,7 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms, const Env
   }
   pl.splits = splits < 1 ? 1 : splits;
   pl.workspace_bytes = 0;
+  pl.b_evict = 0;
   pl.streamk = 0;
   pl.streamk_pure = 0;
   pl.pair = 0;
@@ -1554,10 +1627,13 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
     attr_done[dev] = true;
   }
   const uint64_t K2 = g.K / 2;
-  CUtensorMap ta, tb, tb2;
+  CUtensorMap ta, tb, tb2, tc;
+  // C as bytes: rows of N * 2 bytes at a stride of ldc * 2, boxes of 128 rows x 128 bytes.
   if (!make_operand_map(&ta, g.a, K2, g.M, g.L, g.a_lstride, 128) ||
       !make_operand_map(&tb, g.b, K2, g.N, g.L, g.b_lstride, 128) ||
-      (kDual && !make_operand_map(&tb2, g.b2, K2, g.N, g.L, g.b2_lstride, 128))) {
+      (kDual && !make_operand_map(&tb2, g.b2, K2, g.N, g.L, g.b2_lstride, 128)) ||
+      !make_tma_3d_u8(&tc, g.c, static_cast<uint64_t>(g.N) * 2, g.M, g.L, static_cast<uint64_t>(g.ldc) * 2,
+                      static_cast<uint64_t>(g.c_lstride) * 2, 128, 128)) {
     *why = "cuTensorMapEncodeTiled failed";
     return cudaErrorInvalidValue;
   }
@@ -1581,6 +1657,7 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
   p.group_m = p.tiles_m < 8 ? p.tiles_m : 8;
   p.status = g.status;
   p.inject = g.inject ? 1 : 0;
+  p.b_evict = g.b_evict;
   p.splits = 1;
   p.num_items = p.num_tiles;
   p.streamk = (g.streamk && g.workspace) ? 1 : 0;
@@ -1601,7 +1678,8 @@ static cudaError_t launch_pair(const GemmArgs& g, int num_sms, cudaStream_t stre
     *why = "stream-K workspace too small";
     return cudaErrorInvalidValue;
   }
-  return launch_pdl(gemm_pair_kernel<kDual>, dim3(2 * pairs), dim3(kPairThreads), pair::kSmem, stream, 2, ta, tb, kDual ? tb2 : tb, p);
+  return launch_pdl(gemm_pair_kernel<kDual>, dim3(2 * pairs), dim3(kPairThreads), pair::kSmem, stream, 2, ta, tb,
+                    kDual ? tb2 : tb, tc, p);
 }
 
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why) {

@@ -88,6 +88,7 @@ struct EnvOptions {
   int fault_inject = 0;  // test hook: CTA 0 withholds its first A load
   int gemv_simt = 0;     // NVFP4_GEMV_PATH=simt
   int gemv_ctas = 0;     // > 0 caps the tensor-core GEMV's CTA count (NVFP4_GEMV_CTAS)
+  int b_evict = -1;      // L2 policy of B loads: -1 default, 0 evict_first, 1 normal, 2 evict_last
 };
 EnvOptions read_env_options();
 
@@ -101,6 +102,7 @@ struct GemmArgs {
   int* status;                                     // device status word (bounded-wait timeouts)
   int bn, splits, streamk, streamk_pure, pair;     // from gemm_plan
   int prefetch, inject;                            // from EnvOptions
+  int b_evict;                                     // L2 policy of B loads (0 first, 1 normal, 2 last)
   void* workspace;                                 // stream-K partials + flags (zeroed once; left zeroed)
   size_t workspace_bytes;
 };
@@ -111,6 +113,7 @@ struct GemmPlan {
   int streamk_pure;  // 1: no whole-tile waves before the stream-K ranges (tests / comparison)
   int pair;     // 1: 2-CTA kernel, 256x256 tiles (plain GEMM, M % 256 == 0, N % 256 == 0, no split)
   size_t workspace_bytes;  // stream-K partial slots + flags; 0 otherwise (split K reduces on chip)
+  int b_evict;             // L2 policy of B loads (0 evict_first, 1 normal, 2 evict_last)
 };
 GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms, const EnvOptions& opt);
 cudaError_t launch_gemm(const GemmArgs& g, int num_sms, cudaStream_t stream, const char** why);
