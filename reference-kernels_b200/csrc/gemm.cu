@@ -15,7 +15,7 @@
 //               reads the stage's scale blocks from shared memory and writes
 //               them into its 32 TMEM lanes with tcgen05.st (the blocks
 //               replicated to the four lane quarters, the layout the MMA
-//               reads), then arrives on sf_ready[stage].  tcgen05.cp of the
+//               reads), then arrives on full[stage].  tcgen05.cp of the
 //               same blocks costs ~45 tensor-pipe cycles each and competes
 //               with the MMAs for the pipe (measured); the stores do not.
 //   warp 1      TMEM owner and MMA issuer: per K tile, four tcgen05.mma
@@ -335,7 +335,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sfbuf + S * Cfg::kSfOps * kSfStageBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
-  uint64_t* sf_ready = bars + 2 * S;
   uint64_t* sf_full = bars + 3 * S;  // the stage's scale runs landed (before its A/B tiles, usually)
   uint64_t* acc_full = bars + 4 * S;
   uint64_t* acc_empty = acc_full + Cfg::kAccBufs;
@@ -349,9 +348,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     abort_flag = 0;
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      // full: the producer's expect-tx arrival, the A/B bytes, and one
+      // arrival per scale writer warp once the stage's scales are in TMEM
+      // (the MMA thread waits on this one barrier per K tile).
+      mbar_init(&full[s], 1 + kCopiers);
       mbar_init(&empty[s], 1);
-      mbar_init(&sf_ready[s], kCopiers);
       mbar_init(&sf_full[s], 1);
     }
     for (int b = 0; b < Cfg::kAccBufs; ++b) {
@@ -459,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d0 = tmem_base + acc * Cfg::kAccCols;
         bool ok = true;
         for (int kt = k0; kt < k1; ++kt) {
-          if (!TRW(0, mbar_wait(&full[stage], phase)) || !TRW(1, mbar_wait(&sf_ready[stage], phase))) {
+          if (!TRW(0, mbar_wait(&full[stage], phase))) {
             set_status(p.status, kStatusTimeoutFull);
             abort_flag = 1;
             ok = false;
@@ -551,7 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sf_ready[stage]);
+      if (lane == 0) mbar_arrive(&full[stage]);
       if (++stage == S) {
         stage = 0;
         phase ^= 1;
@@ -794,7 +795,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // and SFB for all 256 columns in its own TMEM, written by its own four
 // writer warps (tcgen05.st) from its own shared memory.  A and B loads signal
 // the leader's full barrier (.cta_group::2 TMA); the writers of both CTAs
-// arrive on the leader's sf_ready barrier; MMA completion is multicast to
+// arrive on the leader's full barrier; MMA completion is multicast to
 // both CTAs' empty / accumulator barriers.  No load uses cluster multicast.
 namespace pair {
 constexpr int kStages = 4;
@@ -891,7 +892,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(outbuf + kOut);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
-  uint64_t* sf_ready = bars + 2 * S;
   uint64_t* sf_full = bars + 3 * S;
   uint64_t* acc_full = bars + 4 * S;
   uint64_t* acc_empty = acc_full + 1;
@@ -909,9 +909,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (threadIdx.x == 0) {
     abort_flag = 0;
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      // The leader's full: its producer's expect-tx arrival, both CTAs' A/B
+      // bytes, and the scale writer warps of both CTAs (one wait per K tile
+      // for the MMA thread).
+      mbar_init(&full[s], 1 + 2 * kPairCopiers);
       mbar_init(&empty[s], 1);
-      mbar_init(&sf_ready[s], 2 * kPairCopiers);  // the leader's: both CTAs' writer warps
       mbar_init(&sf_full[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -1000,7 +1002,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
         tc_fence_after();
         for (int kt = k0; kt < k1; ++kt) {
-          if (!TRW(0, mbar_wait(&full[stage], phase)) || !TRW(1, mbar_wait_cluster(&sf_ready[stage], phase))) {
+          if (!TRW(0, mbar_wait_cluster(&full[stage], phase))) {
             set_status(p.status, kStatusTimeoutFull);
             abort_flag = 1;
             ok = false;
@@ -1027,6 +1029,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (!ok) break;
         tc_commit_pair_mc(acc_full, 0x3);
         TRACE_STAMP(10);
+#ifdef NVFP4_TRACE
+        if (trace[18] == 0) trace[18] = global_timer_ns(); else trace[19] = global_timer_ns();
+#endif
         acc_phase ^= 1;
       }
       tc_commit_pair(drain);
@@ -1038,9 +1043,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     // scale runs into its own TMEM with tcgen05.st, in the layout
     // tcgen05.cp.32x128b.warpx4 would leave (SFA step kk at column 4*kk; SFB
     // block j of step kk at 16 + 4*(2*kk + j)), then arrive on the leader's
-    // sf_ready[stage], which the leader's MMA thread waits for.
+    // full[stage], which the leader's MMA thread waits for.
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t ready0 = map_peer(smem_u32(sf_ready), 0);
+    const uint32_t ready0 = map_peer(smem_u32(full), 0);
     int stage = 0;
     uint32_t phase = 0;
     int total = 0;
@@ -1099,23 +1104,54 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
       tc_fence_after();
       const int rloc = q * 32 + lane;
-      const int row = mb * 256 + static_cast<int>(rank) * 128 + rloc;
-      __half* crow = p.c + l * p.c_lstride + static_cast<int64_t>(row) * p.ldc + static_cast<int64_t>(nb) * (kDual ? 128 : 256);
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-#ifdef NVFP4_TRACE
-      const long long epi_t0 = clock64();
-#endif
-      if (!p.streamk) {
-        // Whole tile (the common case): TMEM -> fp16 -> swizzled staging in
-        // shared memory; the accumulator is released as soon as TMEM has been
-        // read, and one thread stores the staged boxes to C with TMA while
-        // the next tile's MMAs run.  The previous tile's stores must have
-        // finished reading the staging buffer first.
+      // Every epilogue writes its results into the staging buffer in shared
+      // memory, releases the accumulator as soon as TMEM has been read, and
+      // one thread (64) stores the buffer with TMA / bulk copies while the
+      // next item's MMAs run.  Before writing the buffer, the previous
+      // item's stores must have finished reading it.
+      auto stage_wait = [&]() {
         if (threadIdx.x == 64) bulk_wait_group_read0();
         epi_bar();
-        constexpr int kChunks = kDual ? 4 : 8;  // 32-column chunks of this CTA's output rows
-        uint8_t* srow = outbuf + rloc * 128;
+      };
+      constexpr int kChunks = kDual ? 4 : 8;  // 32-column chunks of this CTA's output rows
+      // fp16 output chunk o (32 columns = 64 bytes = four 16-byte units of
+      // the row in box o / 2, units 4 * (o % 2) .. +3, at unit u ^ (row % 8)).
+      auto stage_half = [&](int o, const uint32_t (&r)[32]) {
+        uint8_t* box = outbuf + (o >> 1) * kOutBox + rloc * 128;
         const int sw = rloc & 7;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 v;
+          __half2 h0 = __floats2half2_rn(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
+          __half2 h1 = __floats2half2_rn(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
+          __half2 h2 = __floats2half2_rn(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
+          __half2 h3 = __floats2half2_rn(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
+          v.x = *reinterpret_cast<uint32_t*>(&h0);
+          v.y = *reinterpret_cast<uint32_t*>(&h1);
+          v.z = *reinterpret_cast<uint32_t*>(&h2);
+          v.w = *reinterpret_cast<uint32_t*>(&h3);
+          const int u = 4 * (o & 1) + j;
+          *reinterpret_cast<uint4*>(box + ((u ^ sw) << 4)) = v;
+        }
+      };
+      // Release the accumulator and store the staged fp16 tile to C.
+      auto release_and_store_c = [&]() {
+        tc_fence_before();
+        mbar_arrive_cluster_relaxed(acc_empty0);
+        fence_proxy_async_smem();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const int y = mb * 256 + static_cast<int>(rank) * 128;
+          const int x = nb * (kDual ? 128 : 256) * 2;  // bytes
+#pragma unroll
+          for (int bx = 0; bx < kChunks / 2; ++bx) tma_store_3d(&tm_c, outbuf + bx * kOutBox, x + bx * 128, y, l);
+          bulk_commit_group();
+        }
+      };
+      if (!p.streamk) {
+        // Whole tile (the common case).
+        stage_wait();
 #pragma unroll 1
         for (int o = 0; o < kChunks; ++o) {
           uint32_t r[32];
@@ -1130,64 +1166,54 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           } else {
             tmem_wait_ld();
           }
-          // 32 columns = 64 bytes = four 16-byte units of the row in box
-          // o / 2, units 4 * (o % 2) .. +3, at unit position u ^ (row % 8).
-          uint8_t* box = srow + (o >> 1) * kOutBox;
+          stage_half(o, r);
+        }
+        release_and_store_c();
+      } else if (k0 > 0) {
+        // Contributor: this CTA's 128 rows of the partial tile (fp32) to its
+        // slot, laid out [column group][float4 index][row][4 floats] (16 KB
+        // per 32-column group), staged in shared memory in that layout and
+        // written by bulk stores four groups (64 KB) at a time; then its flag.
+        float* slot_base = p.sk_partial + static_cast<int64_t>(my_slot) * (128 * 256);
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          stage_wait();
+          float4* stg = reinterpret_cast<float4*>(outbuf) + rloc;
+#pragma unroll 1
+          for (int gi = 0; gi < 4; ++gi) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tacc + (4 * h + gi) * 32, r);
+            tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 v;
-            __half2 h0 = __floats2half2_rn(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
-            __half2 h1 = __floats2half2_rn(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
-            __half2 h2 = __floats2half2_rn(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
-            __half2 h3 = __floats2half2_rn(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
-            v.x = *reinterpret_cast<uint32_t*>(&h0);
-            v.y = *reinterpret_cast<uint32_t*>(&h1);
-            v.z = *reinterpret_cast<uint32_t*>(&h2);
-            v.w = *reinterpret_cast<uint32_t*>(&h3);
-            const int u = 4 * (o & 1) + j;
-            *reinterpret_cast<uint4*>(box + ((u ^ sw) << 4)) = v;
+            for (int i = 0; i < 8; ++i)
+              stg[(gi * 8 + i) * 128] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                                    __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+          }
+          if (h == 1) {
+            tc_fence_before();
+            mbar_arrive_cluster_relaxed(acc_empty0);
+          }
+          fence_proxy_async_smem();
+          epi_bar();
+          if (threadIdx.x == 64) {
+            bulk_store(slot_base + h * (128 * 128), outbuf, 128 * 128 * 4);
+            bulk_commit_group();
           }
         }
-        tc_fence_before();
-        mbar_arrive_cluster_relaxed(acc_empty0);
-        fence_proxy_async_smem();
-        epi_bar();
         if (threadIdx.x == 64) {
-          const int y = mb * 256 + static_cast<int>(rank) * 128;
-          const int x = nb * (kDual ? 128 : 256) * 2;  // bytes
-#pragma unroll
-          for (int bx = 0; bx < kChunks / 2; ++bx) tma_store_3d(&tm_c, outbuf + bx * kOutBox, x + bx * 128, y, l);
-          bulk_commit_group();
-        }
-#ifdef NVFP4_TRACE
-        trace[17] += clock64() - epi_t0;
-#endif
-      } else if (k0 > 0) {
-        // Contributor: this CTA's 128 rows of the partial tile to its slot
-        // ([column group][float4 index][row][4] floats), then its flag.
-        float4* dst = reinterpret_cast<float4*>(p.sk_partial) + static_cast<int64_t>(my_slot) * (128 * 256 / 4) + rloc;
-#pragma unroll 1
-        for (int c0 = 0; c0 < 256; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tacc + c0, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            dst[((c0 / 32) * 8 + i) * 128] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                                         __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
-        }
-        tc_fence_before();
-        mbar_arrive_cluster_relaxed(acc_empty0);
-        epi_bar();
-        if (threadIdx.x == 64) {
+          bulk_wait_group0();  // the partial is in global memory
+          fence_proxy_async_all();
           __threadfence();
           st_release_gpu(p.sk_flag + my_slot, 1);
+#ifdef NVFP4_TRACE
+          g_gemm_trace[blockIdx.x * 32 + 22] = global_timer_ns();
+#endif
         }
       } else {
         // Whole tile, or the finaliser of a tile whose K tiles [k1, KT)
         // the following pairs [pair_id + 1, c_end) computed.
         int c_end = pair_id + 1;
-        if (p.streamk && k1 < KT) {
+        if (k1 < KT) {
           const int64_t tile_end = sk_tile_end(p, t, KT);
           while (c_end < npairs && sk_begin(p, c_end, npairs) < tile_end) ++c_end;
           bool ok = true;
@@ -1198,6 +1224,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               for (int c = pair_id + 1; c < c_end; ++c) p.sk_flag[2 * c + rank] = 0;  // ready for the next launch
             else
               set_status(p.status, kStatusTimeoutPeer);
+            fence_proxy_async_all();
+#ifdef NVFP4_TRACE
+            g_gemm_trace[blockIdx.x * 32 + 20] = global_timer_ns();
+#endif
           }
           if (!epi_all(ok)) {
             abort_flag = 1;
@@ -1214,8 +1244,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         for (int c = pair_id + 1; c < c_end; ++c)
           if (sk_has_range(p, c, npairs) && nc < kMaxContrib) contrib[nc++] = c;
         constexpr int kHalves = kDual ? 2 : 1;  // accumulator groups per output chunk
-        constexpr int kOut = kDual ? 4 : 8;     // 32-column output chunks
-        const int nchunks = kOut * kHalves * nc;
+        const int nchunks = kChunks * kHalves * nc;
         auto issue = [&](int q) {  // chunk q -> ring buffer q % kFixBufs
           const int j = q % nc, h = (q / nc) % kHalves, o = q / (nc * kHalves);
           const int g = o + h * 4;
@@ -1225,12 +1254,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           bulk_load(smem + (q % kFixBufs) * kFixChunk, src, kFixChunk, &fix_full[q % kFixBufs],
                     policy_evict_first());
         };
+        stage_wait();
         if (threadIdx.x == 64)
           for (int q = 0; q < nchunks && q < kFixBufs; ++q) issue(q);
         bool fix_ok = true;
         int q = 0;
 #pragma unroll 1
-        for (int o = 0; o < kOut; ++o) {
+        for (int o = 0; o < kChunks; ++o) {
           uint32_t r[kHalves][32];
 #pragma unroll
           for (int h = 0; h < kHalves; ++h) {
@@ -1238,15 +1268,23 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             tmem_wait_ld();
             for (int j = 0; j < nc; ++j, ++q) {
               fix_ok &= mbar_wait(&fix_full[q % kFixBufs], (q / kFixBufs) & 1);
+#ifdef NVFP4_TRACE
+              if (threadIdx.x == 64 && q == 0) g_gemm_trace[blockIdx.x * 32 + 23] = global_timer_ns();
+              if (threadIdx.x == 64 && q == nchunks - 1) g_gemm_trace[blockIdx.x * 32 + 24] = global_timer_ns();
+#endif
               const float4* buf = reinterpret_cast<const float4*>(smem + (q % kFixBufs) * kFixChunk) + rloc;
               float4 v[8];
 #pragma unroll
               for (int i = 0; i < 8; ++i) v[i] = buf[i * 128];
-              // Every thread has read buffer q: refill it with chunk q + kFixBufs.
-              epi_bar();
-              if (threadIdx.x == 64 && q + kFixBufs < nchunks) {
-                fence_proxy_async_smem();
-                issue(q + kFixBufs);
+              // With more chunks than ring buffers: every thread has read
+              // buffer q, refill it with chunk q + kFixBufs.  (Usually one
+              // contributor: all chunks were issued up front, no refills.)
+              if (nchunks > kFixBufs) {
+                epi_bar();
+                if (threadIdx.x == 64 && q + kFixBufs < nchunks) {
+                  fence_proxy_async_smem();
+                  issue(q + kFixBufs);
+                }
               }
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
@@ -1262,13 +1300,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             for (int i = 0; i < 32; ++i)
               r[0][i] = __float_as_uint(silu_mul(__uint_as_float(r[0][i]), __uint_as_float(r[kHalves - 1][i])));
           }
-          store_half_row32(crow + o * 32, r[0]);
+          stage_half(o, r[0]);
         }
         if (!fix_ok) set_status(p.status, kStatusTimeoutPeer);
-        // tcgen05.wait::ld completed the reads; a relaxed arrive suffices
-        // (see the scale writers).
-        tc_fence_before();
-        mbar_arrive_cluster_relaxed(acc_empty0);
+        release_and_store_c();
+#ifdef NVFP4_TRACE
+        if (threadIdx.x == 64) g_gemm_trace[blockIdx.x * 32 + 21] = global_timer_ns();
+#endif
       }
       acc_phase ^= 1;
     }
