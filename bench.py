@@ -50,6 +50,7 @@ PROFILE_NAMES = {
     "gemv": "gemv_tc_kernel_M7168_K16384_L4",
     "gemm": "gemm_pair_kernel_M1024_N7168_K16384",
     "dual": "dual_gemm_kernel_M256_N4096_K7168",
+    "gemm_square": "gemm_pair_kernel_M16384_N16384_K16384",
 }
 
 
