@@ -89,6 +89,12 @@ __device__ __forceinline__ void tmem_ld_32x32b_x1(uint32_t taddr, uint32_t& r) {
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
 // AND of `pred` over the 128 epilogue threads (named barrier 1).
 __device__ __forceinline__ bool epi_all(bool pred) {
   uint32_t out;
@@ -307,12 +313,14 @@ __global__ void __launch_bounds__(gemvtc::kThreads, 1)
         const int slot = blockIdx.x - first;
         float* wsb = p.ws + static_cast<int64_t>(blk) * p.slots * kBM;
         wsb[slot * kBM + r] = x;
-        __threadfence();
+        // The named barrier orders the 128 partial-sum stores before thread
+        // 64's arrival, whose release (cumulative) publishes them; the last
+        // arriver's acquire, passed on by the second barrier, orders its
+        // CTA's reads after every contributor's stores.  (No full fences.)
         epi_bar();
-        if (threadIdx.x == 64) last_flag = (atomicAdd(&p.counters[blk], 1) == last - first);
+        if (threadIdx.x == 64) last_flag = (atom_add_acq_rel_gpu(&p.counters[blk], 1) == last - first);
         epi_bar();
         if (last_flag) {
-          __threadfence();
           float s = 0.f;
           for (int j = 0; j <= last - first; ++j) s += __ldcg(&wsb[j * kBM + r]);
           *crow = __float2half_rn(s);
