@@ -1255,52 +1255,111 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                     policy_evict_first());
         };
         stage_wait();
-        if (threadIdx.x == 64)
-          for (int q = 0; q < nchunks && q < kFixBufs; ++q) issue(q);
         bool fix_ok = true;
-        int q = 0;
+        if (!kDual) {
+          // One contributor at a time: its whole partial (eight contiguous
+          // 16 KB column groups) in one bulk copy, added into the
+          // accumulator in TMEM (tcgen05.ld, add, tcgen05.st) -- or, for the
+          // last contributor, staged as fp16 for C.  Contributors are added
+          // in pair order, the same order on every call.  (A ring of 16 KB
+          // copies waited one by one cost ~0.7 us per chunk.)
+          if (nc == 0) {
 #pragma unroll 1
-        for (int o = 0; o < kChunks; ++o) {
-          uint32_t r[kHalves][32];
-#pragma unroll
-          for (int h = 0; h < kHalves; ++h) {
-            tmem_ld_32x32b_x32(tacc + o * 32 + h * 128, r[h]);
-            tmem_wait_ld();
-            for (int j = 0; j < nc; ++j, ++q) {
-              fix_ok &= mbar_wait(&fix_full[q % kFixBufs], (q / kFixBufs) & 1);
+            for (int o = 0; o < kChunks; ++o) {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(tacc + o * 32, r);
+              tmem_wait_ld();
+              stage_half(o, r);
+            }
+          }
+#pragma unroll 1
+          for (int j = 0; j < nc; ++j) {
+            if (threadIdx.x == 64) {
+              mbar_arrive_expect_tx(&fix_full[j % kFixBufs], 8 * kFixChunk);
+              bulk_load(smem,
+                        reinterpret_cast<const uint8_t*>(p.sk_partial) +
+                            static_cast<int64_t>(2 * contrib[j] + rank) * 8 * kFixChunk,
+                        8 * kFixChunk, &fix_full[j % kFixBufs], policy_evict_first());
+            }
+            fix_ok &= mbar_wait(&fix_full[j % kFixBufs], (j / kFixBufs) & 1);
 #ifdef NVFP4_TRACE
-              if (threadIdx.x == 64 && q == 0) g_gemm_trace[blockIdx.x * 32 + 23] = global_timer_ns();
-              if (threadIdx.x == 64 && q == nchunks - 1) g_gemm_trace[blockIdx.x * 32 + 24] = global_timer_ns();
+            if (threadIdx.x == 64 && j == 0) g_gemm_trace[blockIdx.x * 32 + 23] = global_timer_ns();
 #endif
-              const float4* buf = reinterpret_cast<const float4*>(smem + (q % kFixBufs) * kFixChunk) + rloc;
+            const bool last_c = j == nc - 1;
+#pragma unroll 1
+            for (int o = 0; o < kChunks; ++o) {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(tacc + o * 32, r);
+              const float4* buf = reinterpret_cast<const float4*>(smem + o * kFixChunk) + rloc;
               float4 v[8];
 #pragma unroll
               for (int i = 0; i < 8; ++i) v[i] = buf[i * 128];
-              // With more chunks than ring buffers: every thread has read
-              // buffer q, refill it with chunk q + kFixBufs.  (Usually one
-              // contributor: all chunks were issued up front, no refills.)
-              if (nchunks > kFixBufs) {
-                epi_bar();
-                if (threadIdx.x == 64 && q + kFixBufs < nchunks) {
-                  fence_proxy_async_smem();
-                  issue(q + kFixBufs);
-                }
-              }
+              tmem_wait_ld();
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
-                r[h][4 * i] = __float_as_uint(__uint_as_float(r[h][4 * i]) + v[i].x);
-                r[h][4 * i + 1] = __float_as_uint(__uint_as_float(r[h][4 * i + 1]) + v[i].y);
-                r[h][4 * i + 2] = __float_as_uint(__uint_as_float(r[h][4 * i + 2]) + v[i].z);
-                r[h][4 * i + 3] = __float_as_uint(__uint_as_float(r[h][4 * i + 3]) + v[i].w);
+                r[4 * i] = __float_as_uint(__uint_as_float(r[4 * i]) + v[i].x);
+                r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) + v[i].y);
+                r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) + v[i].z);
+                r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) + v[i].w);
               }
+              if (last_c)
+                stage_half(o, r);
+              else
+                tmem_st_32x32b_x32(tacc + o * 32, r);
+            }
+            if (!last_c) {
+              // Partial sums back in TMEM, and every thread done reading the
+              // buffer before the next contributor's copy overwrites it.
+              tmem_wait_st();
+              fence_proxy_async_smem();
+              epi_bar();
             }
           }
-          if (kDual) {
+#ifdef NVFP4_TRACE
+          if (threadIdx.x == 64) g_gemm_trace[blockIdx.x * 32 + 24] = global_timer_ns();
+#endif
+        } else {
+          // Dual GEMM: both accumulator halves per output chunk, streamed as
+          // 16 KB chunks (one per contributor and 32-column group) through
+          // a ring of kFixBufs buffers.
+          if (threadIdx.x == 64)
+            for (int q = 0; q < nchunks && q < kFixBufs; ++q) issue(q);
+          int q = 0;
+#pragma unroll 1
+          for (int o = 0; o < kChunks; ++o) {
+            uint32_t r[kHalves][32];
+#pragma unroll
+            for (int h = 0; h < kHalves; ++h) {
+              tmem_ld_32x32b_x32(tacc + o * 32 + h * 128, r[h]);
+              tmem_wait_ld();
+              for (int j = 0; j < nc; ++j, ++q) {
+                fix_ok &= mbar_wait(&fix_full[q % kFixBufs], (q / kFixBufs) & 1);
+                const float4* buf = reinterpret_cast<const float4*>(smem + (q % kFixBufs) * kFixChunk) + rloc;
+                float4 v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = buf[i * 128];
+                if (nchunks > kFixBufs) {
+                  // every thread has read buffer q: refill it with chunk q + kFixBufs
+                  epi_bar();
+                  if (threadIdx.x == 64 && q + kFixBufs < nchunks) {
+                    fence_proxy_async_smem();
+                    issue(q + kFixBufs);
+                  }
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  r[h][4 * i] = __float_as_uint(__uint_as_float(r[h][4 * i]) + v[i].x);
+                  r[h][4 * i + 1] = __float_as_uint(__uint_as_float(r[h][4 * i + 1]) + v[i].y);
+                  r[h][4 * i + 2] = __float_as_uint(__uint_as_float(r[h][4 * i + 2]) + v[i].z);
+                  r[h][4 * i + 3] = __float_as_uint(__uint_as_float(r[h][4 * i + 3]) + v[i].w);
+                }
+              }
+            }
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               r[0][i] = __float_as_uint(silu_mul(__uint_as_float(r[0][i]), __uint_as_float(r[kHalves - 1][i])));
+            stage_half(o, r[0]);
           }
-          stage_half(o, r[0]);
         }
         if (!fix_ok) set_status(p.status, kStatusTimeoutPeer);
         release_and_store_c();
