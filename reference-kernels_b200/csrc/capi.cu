@@ -89,6 +89,14 @@ static void* workspace_for(int kind, int dev, size_t bytes, cudaStream_t stream,
   std::lock_guard<std::mutex> lock(g_ws_mutex);
   DeviceWorkspace& w = g_ws[kind][dev];
   if (w.bytes >= bytes) return w.ptr;
+  // Growing the workspace synchronises the device and allocates, neither of
+  // which a stream capture allows: make one uncaptured call of the largest
+  // shape first.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone) {
+    *err = cudaErrorStreamCaptureUnsupported;
+    return nullptr;
+  }
   if (w.ptr) {
     // earlier launches may still read the old buffer
     if ((*err = cudaDeviceSynchronize()) != cudaSuccess) return nullptr;
@@ -197,7 +205,12 @@ NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa_blk, cons
     g.workspace_bytes = gemv_tc_workspace_bytes(M, K, L, ctas);
     cudaError_t e = cudaSuccess;
     g.workspace = workspace_for(kWsGemv, dev, g.workspace_bytes, s, &e);
-    if (!g.workspace) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: workspace: %s", cudaGetErrorString(e));
+    if (!g.workspace)
+      return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: workspace: %s",
+                  e == cudaErrorStreamCaptureUnsupported
+                      ? "it must grow, which a stream capture does not allow; make one uncaptured call of this shape "
+                        "first"
+                      : cudaGetErrorString(e));
     g.status = status_ptr(dev);
     g.inject = opt.fault_inject;
     const char* why = nullptr;
@@ -255,7 +268,12 @@ static int apply_plan(const char* who, int dev, const GemmPlan& pl, GemmArgs& g,
   if (pl.workspace_bytes) {
     cudaError_t we;
     g.workspace = workspace_for(kWsGemm, dev, pl.workspace_bytes, static_cast<cudaStream_t>(stream), &we);
-    if (!g.workspace) return fail(NVFP4_ERR_CUDA, "%s: workspace: %s", who, cudaGetErrorString(we));
+    if (!g.workspace)
+      return fail(NVFP4_ERR_CUDA, "%s: workspace: %s", who,
+                  we == cudaErrorStreamCaptureUnsupported
+                      ? "it must grow, which a stream capture does not allow; make one uncaptured call of this shape "
+                        "first"
+                      : cudaGetErrorString(we));
     g.workspace_bytes = pl.workspace_bytes;
   }
   return NVFP4_OK;

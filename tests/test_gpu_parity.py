@@ -245,3 +245,29 @@ def test_k_tail(problem, m, n, k, l, kernel, monkeypatch):
     data = inputs.baseline_input(problem, m, k, l, 66, n=n)
     out = run(problem, data).clone()
     assert_match(out, oracle_ref(problem, data), f"{problem} {kernel} {m}x{n}x{k}x{l} K tail vs oracle")
+
+
+def test_workspace_growth_inside_capture_is_refused_then_works_uncaptured():
+    """A call that would have to grow the library's per-device workspace
+    inside a CUDA-graph capture returns an error before enqueuing anything
+    (the capture stays valid); the same call outside a capture grows the
+    workspace and is correct, and then captures and replays correctly."""
+    from nvfp4_b200 import _lib
+    m, k, l = 128 * 4096, 256, 4  # 16384 row blocks: a 16 MB workspace, larger than any other test's
+    data = inputs.baseline_input("gemv", m, k, l, 8)
+    ops._CACHE.clear()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        with pytest.raises(_lib.Nvfp4Error, match="stream capture"):
+            ops.gemv(data)
+    torch.cuda.synchronize()
+    out = run("gemv", data).clone()
+    assert_match(out, scaled_mm_ref("gemv", data), "gemv after workspace growth")
+    data[-1].zero_()
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2):
+        ops.gemv(data)
+    g2.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(data[-1], out)
