@@ -1,14 +1,15 @@
 """Generates the golden fixtures under tests/golden/ on a CUDA B200.
 
-For each case it draws the reference's own inputs (nvfp4_b200.inputs.reference_input,
-which replays the RNG calls of problems/nvidia/*/reference.py:generate_input
-on the CUDA device, so the tensors equal the reference's for that seed) and
-computes ref_kernel through torch._scaled_mm exactly as
-problems/nvidia/*/reference.py does.  Inputs (plain-layout bytes) and the
-fp16 outputs are stored as .npz; tests/test_oracle.py checks the CPU oracle
-against them without a GPU.
+For each case it imports the reference's own problems/nvidia/nvfp4_*/reference.py
+from the baseline/_ref copy (baseline/install_reference.py, baseline/refload.py),
+draws the inputs with its generate_input and computes the outputs with its
+ref_kernel (torch._scaled_mm -> cuBLASLt).  Inputs (plain-layout bytes) and
+the fp16 outputs are stored as .npz, with `meta` naming the reference files
+and the library versions; tests/test_oracle.py checks the CPU oracle against
+them without a GPU.
 
-Usage (on a GPU box):  python tests/golden/make_golden.py --out tests/golden
+Usage (on a GPU box, with baseline/_ref installed):
+    python tests/golden/make_golden.py --out tests/golden
 """
 import argparse
 import os
@@ -21,8 +22,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "reference-kernels_b200"))
 
-from nvfp4_b200 import inputs  # noqa: E402
-from tests.refcheck import scaled_mm_ref  # noqa: E402
+sys.path.insert(0, os.path.join(ROOT, "baseline"))
+import refload  # noqa: E402
 
 CASES = [
     ("gemv", dict(m=128, k=256, l=1, seed=1111)),
@@ -43,13 +44,16 @@ def main():
     ap.add_argument("--out", default=os.path.join(ROOT, "tests", "golden"))
     args = ap.parse_args()
     os.makedirs(args.out, exist_ok=True)
-    meta = f"torch {torch.__version__}, {torch.cuda.get_device_name(0)}, cuda {torch.version.cuda}"
+    versions = f"torch {torch.__version__}, {torch.cuda.get_device_name(0)}, cuda {torch.version.cuda}"
     for problem, kw in CASES:
         kw = dict(kw)
-        n = kw.pop("n", None)
-        data = inputs.reference_input(problem, n=n, device="cuda", **kw)
-        out = scaled_mm_ref(problem, data)
+        ref = refload.load(problem)
+        src = f"problems/nvidia/{refload.PROBLEM_DIRS[problem]}/reference.py"
+        meta = f"inputs: {src} generate_input{tuple(kw.items())}; out: {src} ref_kernel; {versions}"
+        data = ref.generate_input(**kw)
+        out = ref.ref_kernel(tuple(t.clone() for t in data))
         torch.cuda.synchronize()
+        n = kw.pop("n", None)
         if problem == "dual":
             a, b1, b2, sfa, sfb1, sfb2 = data[:6]
             arrays = dict(a=u8(a), b1=u8(b1), b2=u8(b2), sfa=u8(sfa), sfb1=u8(sfb1), sfb2=u8(sfb2))
