@@ -123,6 +123,11 @@ struct GemmConfig {
   static constexpr int kSfCols = 16 * kSfOps;                         // TMEM columns of scales per stage
   static constexpr int kTmemCols = 512;
   static_assert(kAccBufs * kAccCols + kStages * kSfCols <= kTmemCols, "TMEM budget");
+  // A producer waits on empty[stage] by phase parity, which is only exact
+  // while no stage can be two laps ahead of the MMA; a producer's previous
+  // wait (K tile g - kProducers) covers K tile g - kProducers - kStages, so
+  // that holds only when kProducers <= kStages.
+  static_assert(kProducers <= kStages, "more producer warps than stages breaks the parity waits");
   static constexpr int kTxBytes = kStageBytes;                 // full[]: A and B tiles
   static constexpr int kSmemBytes =
       1024 /*align slack*/ + kStages * (kStageBytes + kSfOps * kSfStageBytes) + 256 /*barriers*/;
@@ -809,6 +814,7 @@ constexpr int kAccCols = 256;
 constexpr int kSfCols = 48;
 constexpr int kTmemCols = 512;
 static_assert(kAccCols + kStages * kSfCols <= kTmemCols, "TMEM budget");
+static_assert(kProducers <= kStages, "more producer warps than stages breaks the parity waits");
 static_assert(kStage % 1024 == 0, "stage alignment");
 constexpr int kFixBufs = 8;          // stream-K finaliser ring: 8 x 16 KB in the stage area
 constexpr int kFixChunk = 16 * 1024;  // one (contributor, 32-column group) of a partial slot
