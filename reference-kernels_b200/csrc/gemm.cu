@@ -329,7 +329,8 @@ __device__ __forceinline__ void share_groups(int ngroups, int S, int s, int& g0,
 template <int BN, bool kDual>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                const __grid_constant__ CUtensorMap tm_b2, const GemmParams p) {
+                const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_c,
+                const GemmParams p) {
   if (threadIdx.x == 0) TRACE_STAMP(8);
   using Cfg = GemmConfig<BN, kDual>;
   constexpr int S = Cfg::kStages;
@@ -731,8 +732,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (epi && ok) {
       int mb, nb, l;
       tile_coords(p, t, mb, nb, l);
-      const int row = mb * kBM + rloc;
-      __half* crow = p.c + l * p.c_lstride + static_cast<int64_t>(row) * p.ldc + static_cast<int64_t>(nb) * BN;
+      // This rank's share of C, 32-column groups of 128 rows x 64 bytes,
+      // staged after the receive slots and written by TMA stores (one box
+      // per group; measured the same speed as 64-byte row pieces stored by
+      // every thread, and the stores leave the SM as a few bulk requests).
+      const uint32_t recv_bytes = static_cast<uint32_t>((S - 1) * max_share * (GF / 4) * kBM * 16);
+      uint8_t* out_stage = tiles + ((recv_bytes + 1023u) & ~1023u);
       int g0, g1;
       share_groups(NG, S, rank, g0, g1);
       const float4* recv = reinterpret_cast<const float4*>(tiles);
@@ -767,7 +772,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i)
           res[i] = __float_as_uint(kDual ? silu_mul(acc[0][i], acc[Cfg::kNB - 1][i]) : acc[0][i]);
-        store_half_row32(crow + g * 32, res);
+        uint4* dst = reinterpret_cast<uint4*>(out_stage + (g - g0) * (kBM * 64) + rloc * 64);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          __half2 h0 = __floats2half2_rn(__uint_as_float(res[8 * j + 0]), __uint_as_float(res[8 * j + 1]));
+          __half2 h1 = __floats2half2_rn(__uint_as_float(res[8 * j + 2]), __uint_as_float(res[8 * j + 3]));
+          __half2 h2 = __floats2half2_rn(__uint_as_float(res[8 * j + 4]), __uint_as_float(res[8 * j + 5]));
+          __half2 h3 = __floats2half2_rn(__uint_as_float(res[8 * j + 6]), __uint_as_float(res[8 * j + 7]));
+          dst[j] = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                              *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+        }
+      }
+      fence_proxy_async_smem();
+      epi_bar();
+      if (threadIdx.x == 64) {
+        for (int g = g0; g < g1; ++g)
+          tma_store_3d(&tm_c, out_stage + (g - g0) * (kBM * 64), (nb * BN + g * 32) * 2, mb * kBM, l);
+        bulk_commit_group();
+        bulk_wait_group0();  // complete before the CTA exits
       }
     }
   }
@@ -1523,11 +1545,14 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }
-  CUtensorMap ta, tb, tb2;
+  CUtensorMap ta, tb, tb2, tc;
   const int K2 = g.K / 2;
+  // C as bytes for the split-K epilogue: boxes of 128 rows x 64 bytes (32 columns), no swizzle.
   if (!make_operand_map(&ta, g.a, K2, g.M, g.L, g.a_lstride, kBM) ||
       !make_operand_map(&tb, g.b, K2, g.N, g.L, g.b_lstride, BN) ||
-      (kDual && !make_operand_map(&tb2, g.b2, K2, g.N, g.L, g.b2_lstride, BN))) {
+      (kDual && !make_operand_map(&tb2, g.b2, K2, g.N, g.L, g.b2_lstride, BN)) ||
+      !make_tma_3d_u8(&tc, g.c, static_cast<uint64_t>(g.N) * 2, g.M, g.L, static_cast<uint64_t>(g.ldc) * 2,
+                      static_cast<uint64_t>(g.c_lstride) * 2, 64, kBM)) {
     *why = "cuTensorMapEncodeTiled failed";
     return cudaErrorInvalidValue;
   }
@@ -1573,7 +1598,7 @@ static cudaError_t launch_impl(const GemmArgs& g, int num_sms, cudaStream_t stre
     return cudaErrorInvalidValue;
   }
   return launch_pdl(gemm_kernel<BN, kDual>, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, stream, p.splits, ta, tb,
-                    tb2, p);
+                    tb2, tc, p);
 }
 
 // Tile width and K splits for a problem.  Problems with fewer tiles than SMs
@@ -1647,6 +1672,19 @@ GemmPlan gemm_plan(int M, int N, int K, int L, bool dual, int num_sms, const Env
                    : (pl.bn == 256 ? max_active_clusters<256, false>(splits) : max_active_clusters<128, false>(splits));
     if (fit < 0) fit = num_sms / splits;
     if (tiles <= fit) break;
+    --splits;
+  }
+  // The split-K exchange reuses the pipeline stages for the receive slots
+  // and, after them, the staged output share: both must fit.
+  while (splits > 1) {
+    const int ng = pl.bn / 32, share = (ng + splits - 1) / splits;
+    const int gf = 32 * (dual ? 2 : 1);
+    const size_t recv = static_cast<size_t>(splits - 1) * share * (gf / 4) * kBM * 16;
+    const size_t need = ((recv + 1023) & ~static_cast<size_t>(1023)) + static_cast<size_t>(share) * kBM * 64;
+    const size_t have = dual ? static_cast<size_t>(GemmConfig<128, true>::kStages) * GemmConfig<128, true>::kStageBytes
+                        : pl.bn == 256 ? static_cast<size_t>(GemmConfig<256, false>::kStages) * GemmConfig<256, false>::kStageBytes
+                                       : static_cast<size_t>(GemmConfig<128, false>::kStages) * GemmConfig<128, false>::kStageBytes;
+    if (need <= have) break;
     --splits;
   }
   pl.splits = splits < 1 ? 1 : splits;

@@ -120,8 +120,9 @@ def test_non_contiguous_output_shard():
     assert torch.count_nonzero(out[:, :n0]) == 0 and torch.count_nonzero(out[:, n1:]) == 0
 
 
-@pytest.mark.parametrize("splits", [2, 3, 5])
-@pytest.mark.parametrize("problem,m,n,k", [("gemm", 256, 512, 2816), ("dual", 256, 384, 2816), ("gemm", 128, 256, 1280)])
+@pytest.mark.parametrize("splits", [2, 3, 5, 7])
+@pytest.mark.parametrize("problem,m,n,k", [("gemm", 256, 512, 2816), ("dual", 256, 384, 2816), ("gemm", 128, 256, 1280),
+                                           ("gemm", 128, 512, 3584)])
 def test_split_k_matches_oracle_and_repeats(problem, m, n, k, splits, monkeypatch):
     """Split-K tiles (partials combined in split order by the last arriver):
     parity with the CPU oracle and bit-identical repeated calls."""
