@@ -272,3 +272,14 @@ def test_workspace_growth_inside_capture_is_refused_then_works_uncaptured():
     g2.replay()
     torch.cuda.synchronize()
     assert torch.equal(data[-1], out)
+
+
+@pytest.mark.parametrize("m,k,l", [(128, 64, 1), (128, 192, 3), (256, 256, 8), (128, 320, 2), (384, 16384 + 256, 1)])
+def test_gemv_edges_against_oracle(m, k, l, gemv_path):
+    """GEMV edge cases: the smallest K (one 64-element scale group of four),
+    K that is not a multiple of 256 (SIMT kernel), many batches, and K one
+    256-wide tile past a power of two (the tensor-core kernel's partial last
+    unit), on both kernels where they apply, against the CPU oracle."""
+    data = inputs.baseline_input("gemv", m, k, l, 17)
+    out = run("gemv", data)
+    assert_match(out, oracle_ref("gemv", data), f"gemv {m}x{k}x{l}")
