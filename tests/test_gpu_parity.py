@@ -283,3 +283,36 @@ def test_gemv_edges_against_oracle(m, k, l, gemv_path):
     data = inputs.baseline_input("gemv", m, k, l, 17)
     out = run("gemv", data)
     assert_match(out, oracle_ref("gemv", data), f"gemv {m}x{k}x{l}")
+
+
+@pytest.mark.parametrize("problem,m,n,k,l", [("gemm", 512, 512, 1024, 2), ("dual", 512, 256, 1024, 3)])
+def test_pair_kernel_batched(problem, m, n, k, l, monkeypatch):
+    """2-CTA tiles over several batch indices (tiles of every batch in one
+    persistent launch) against the CPU oracle."""
+    monkeypatch.setenv("NVFP4_PAIR", "1")
+    data = inputs.baseline_input(problem, m, k, l, 23, n=n)
+    out = run(problem, data)
+    assert_match(out, oracle_ref(problem, data), f"{problem} pair {m}x{n}x{k}x{l}")
+
+
+def test_dual_output_shard_through_the_c_abi():
+    """A dual-GEMM N-shard written through offset B1/B2/scale/C pointers and
+    the full problem's ldc (the multi-GPU path) equals the same columns of
+    the whole problem; columns outside the shard stay untouched."""
+    from nvfp4_b200 import _lib
+    m, n, k = 256, 512, 1024
+    a, b1, b2, sfa, sfb1, sfb2, sfa_p, sfb1_p, sfb2_p, c = inputs.baseline_input("dual", m, k, 1, 29, n=n)
+    full = ops.dual_gemm((a, b1, b2, sfa, sfb1, sfb2, sfa_p, sfb1_p, sfb2_p, c)).clone()
+    torch.cuda.synchronize()
+    out = torch.zeros_like(c)
+    n0, n1 = 256, 512
+    k2 = k // 2
+    lib = _lib.load()
+    _lib.check(lib.nvfp4_dual_gemm(a.data_ptr(), b1.data_ptr() + n0 * k2, b2.data_ptr() + n0 * k2, sfa_p.data_ptr(),
+                                   sfb1_p.data_ptr() + (n0 // 128) * k * 8, sfb2_p.data_ptr() + (n0 // 128) * k * 8,
+                                   out.data_ptr() + n0 * 2, m, n1 - n0, k, 1, a.stride(2), b1.stride(2),
+                                   m * k // 16, n * k // 16, out.stride(0), out.stride(2),
+                                   torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert torch.equal(out[:, n0:n1], full[:, n0:n1])
+    assert torch.count_nonzero(out[:, :n0]) == 0
