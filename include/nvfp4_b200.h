@@ -25,9 +25,11 @@
  *   C               : fp16, row m of slice l at c + l*c_lstride + m*ldc
  *
  * All calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy
- * default stream).  The tensor-core GEMV (always) and the GEMMs (only with
- * stream-K switched on) use a per-device workspace, which the library
- * allocates on the first call that needs it.  Every entry point returns 0 on
+ * default stream).  The tensor-core GEMV (always) and the GEMMs (when the
+ * planner uses stream-K: more tiles than SMs or SM pairs, in an uneven last
+ * wave, e.g. 1024x7168x16384) use a per-device workspace, which the library
+ * allocates on the first call that needs it (a call that would have to grow
+ * it inside a stream capture returns NVFP4_ERR_CUDA and enqueues nothing).  Every entry point returns 0 on
  * success or one of the NVFP4_ERR_* codes; nvfp4_last_error() then returns a
  * message (thread-local).  Nothing runs on the CPU: there is no fallback.
  */
